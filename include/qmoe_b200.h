@@ -1,0 +1,153 @@
+/*
+ * libqmoe_b200 — B200 (sm_100a) kernels for the NVFP4 routed-expert forward and the FP8/NVFP4 dense
+ * GEMVs of the Nemotron-3.5-Super engine (helgard-orlm/nemotron-super-8gb), behind a plain C ABI.
+ *
+ * Conventions shared by every entry point:
+ *   - All pointers are device pointers unless stated; sizes are element counts.
+ *   - `stream` is a cudaStream_t passed as void* (0 = the legacy default stream).
+ *   - Launches are asynchronous on `stream`; nothing synchronises the host.
+ *   - The return value is a status (QMOE_OK or one of QMOE_ERR_*) for argument checks and the
+ *     launch itself. Kernels that wait on other CTAs bound every wait and record a timeout in the
+ *     caller's workspace status word, read with qmoe_workspace_status().
+ *   - Nothing allocates device memory. Kernels that need scratch take a caller workspace whose size
+ *     comes from the matching *_workspace_bytes() function.
+ *   - Expert blocks use the reference's byte format (qmoe_ns.py:9-14, repack.py:3-7):
+ *       up_w [2688,512] u8 @0 | up_s [2688,64] e4m3 @1376256 | dn_w [1024,1344] u8 @1548288 |
+ *       dn_s [1024,168] e4m3 @2924544, BLOCK = 3096576 bytes; two e2m1 per byte, low nibble = even
+ *       element; value = e2m1 * e4m3 * weight_scale_2. The "T" layout (qmoe_ns.py:137-141) keeps the
+ *       up half and stores down as dnT_w [2688 neuron, 512] @1548288 (low nibble = even row) and
+ *       dnT_s [168 group, 1024 row] @2924544.
+ */
+#ifndef QMOE_B200_H
+#define QMOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QMOE_OK 0
+#define QMOE_ERR_SHAPE 1       /* a size or count is out of range */
+#define QMOE_ERR_ALIGN 2       /* a pointer or stride breaks the required alignment */
+#define QMOE_ERR_LAUNCH 3      /* the CUDA launch failed (cudaGetLastError) */
+#define QMOE_ERR_TIMEOUT 4     /* a device-side wait gave up (recorded in the workspace status) */
+#define QMOE_ERR_NULL 5        /* a required pointer is NULL */
+#define QMOE_ERR_DTYPE 6       /* unknown activation dtype code */
+#define QMOE_ERR_DEVICE 7      /* the current device is not an sm_100 part */
+#define QMOE_ERR_WORKSPACE 8   /* workspace too small */
+
+/* activation dtype codes */
+#define QMOE_DT_F32 0
+#define QMOE_DT_BF16 1
+#define QMOE_DT_F16 2
+
+#define QMOE_LAT 1024
+#define QMOE_INTER 2688
+#define QMOE_BLOCK 3096576
+#define QMOE_UPB 1548288
+#define QMOE_MAX_K 65535       /* experts (or pairs) per call; the model routes 22 per token */
+
+/* Library version string and status names. */
+const char *qmoe_version(void);
+const char *qmoe_status_string(int status);
+
+/* Device status word of a workspace (copies 4 bytes to the host and synchronises `stream`).
+ * Returns QMOE_OK or the first device-side error code the kernels recorded; `clear` resets it. */
+int qmoe_workspace_status(void *workspace, int clear, void *stream);
+
+/* ------------------------------------------------------------------ routed experts, decode step */
+
+/* Replaces `_up` (qmoe_ns.py:24-44) as launched by moe_decode / moe_decode_groups
+ * (qmoe_ns.py:74, :248): h[j, n] = relu(s2[j,0] * sum_g up_s[n,g] * sum_{16} e2m1(up_w) * x)^2 for the
+ * expert in slot sidx[j], j < K. slots: base of the slot array (nslots slots), slot_bytes its row stride
+ * (BLOCK or UPB, multiple of 16). x [1024] in x_dtype; s2 [K,2] f32; h [K,2688] f32 out.
+ * A slot index outside [0, nslots) reads nothing and yields NaN for that expert. */
+int qmoe_decode_up(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const int32_t *sidx, int K,
+                   const float *s2, const void *x, int x_dtype, float *h, void *stream);
+
+/* Replaces the live-group glue of moe_decode_groups (qmoe_ns.py:249-251): glive[j,g] = any(h[j,16g:16g+16] > 0),
+ * gcnt[j] = number of live groups, gidx[j] = live groups ascending followed by dead groups ascending
+ * (= the stable descending sort of glive). h [K,2688] f32; gidx [K,168] i32; gcnt [K] i32. */
+int qmoe_live_groups(const float *h, int K, int32_t *gidx, int32_t *gcnt, void *stream);
+
+/* Replaces `_down_groups` (qmoe_ns.py:209-239) with GROUP_CFG's split (qmoe_ns.py:242):
+ * part[s, j, r] = coef[j] * s2[j,1] * sum_{live group g = gidx[j,k], k = s mod KS, k < gcnt[j]}
+ *                 dnT_s[g, r] * sum_{n in g, h[j,n] > 0} e2m1(dnT_w[n, r]) * h[j, n].
+ * tab [K] i64: device addresses of the T-layout blocks; part [KS, K, 1024] f32 out; 1 <= KS <= 8. */
+int qmoe_decode_down_groups(const int64_t *tab, const float *h, const int32_t *gidx, const int32_t *gcnt,
+                            const float *s2, const float *coef, int K, int KS, float *part, void *stream);
+
+/* Replaces `moe_decode_groups` (qmoe_ns.py:245-255), the decode-step routed-expert forward over the
+ * T layout: up GEMV + ReLU^2 (reads slots_up + sidx[j]*slot_bytes), live-group compaction, and the
+ * live-group down GEMV (reads the block at tab[j]), then the fixed-order sum over experts:
+ *   y[r] = sum_j coef[j] * s2[j,1] * (D_j h_j)[r].
+ * Outputs: h [K,2688] f32, gidx [K,168] i32, gcnt [K] i32 (as the reference leaves them), part [K,1024]
+ * f32 per-expert outputs (the reference's part_buf[0,:K]), y [1024] f32. The workspace (size from
+ * qmoe_decode_groups_workspace_bytes) must not be used by another call running concurrently. */
+size_t qmoe_decode_groups_workspace_bytes(int K);
+int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
+                       const int64_t *tab,
+                       const float *s2, const float *coef, const void *x, int x_dtype, int K, float *h,
+                       int32_t *gidx, int32_t *gcnt, float *part, float *y, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/* Replaces `moe_decode` (qmoe_ns.py:70-76), the orig-layout decode forward (full down, no skip):
+ * h [K,2688] f32 out, out [K,1024] f32 out (out[j] = coef[j]*s2[j,1]*D_j h_j), y [1024] = sum_j out[j]
+ * in slot order. slots/slot_bytes as in qmoe_decode_up (slot_bytes = BLOCK). */
+int qmoe_decode(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const int32_t *sidx, const float *s2,
+                const float *coef, const void *x, int x_dtype, int K, float *h, float *out, float *y, void *stream);
+
+/* ------------------------------------------------------------------ routed experts, prompt path */
+
+/* Replaces `moe_pairs` (qmoe_ns.py:127-133, kernels :79-124): P pairs p = (slot pslot[p], token ptok[p]):
+ * h[p] = relu(s2p[p,0] * U_slot X[ptok[p]])^2, out[p] = coefp[p] * s2p[p,1] * D_slot h[p].
+ * X [T,1024] in x_dtype (T > max ptok); h [P,2688] f32 out; out [P,1024] f32 out. Orig layout. */
+int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const int32_t *pslot, const int32_t *ptok,
+               const float *s2p, const float *coefp, const void *X, int x_dtype, int T, int P, float *h, float *out,
+               void *stream);
+
+/* ------------------------------------------------------------------ layouts */
+
+/* Replaces `from_T_fast` (qmoe_ns.py:345-353, kernel `_fromT_w` :327-342): N blocks (stride BLOCK)
+ * converted from the T layout to the orig layout in place. scratch >= N * 1376256 bytes. */
+int qmoe_from_T(uint8_t *blks, int N, uint8_t *scratch, void *stream);
+
+/* Replaces `to_T_batch` (repack_T.py:27-35; qmoe_ns.py:356-364 per block): orig -> T in place.
+ * scratch >= N * 1376256 bytes. */
+int qmoe_to_T(uint8_t *blks, int N, uint8_t *scratch, void *stream);
+
+/* Replaces `deq` (qmoe_ns.py:395-404): w [N, K/2] u8 codes, s [N, K/16] e4m3 -> out [N, K] fp32 =
+ * (e2m1 * e4m3) * ws2, bit-exact with the reference. K a multiple of 16. */
+int qmoe_deq(const uint8_t *w, const uint8_t *s, float ws2, int64_t N, int64_t K, float *out, void *stream);
+
+/* Replaces `block_deq` (qmoe_ns.py:407-412, via deq :395-404): one orig-layout block -> up [2688,1024]
+ * and down [1024,2688] fp32 = (e2m1 * e4m3) * s2. Bit-exact with the reference. */
+int qmoe_block_deq(const uint8_t *blk, float s2_up, float s2_down, float *up, float *down, void *stream);
+
+/* ------------------------------------------------------------------ dense quantized linears */
+
+/* Replaces `_gemv_fp8` / `_gemv_fp8_m2` (dense_q.py:35-53, :83-103) as dispatched by gemv / gemv_mb
+ * (dense_q.py:139-152, :199-212): y[m, n] = s * sum_k e4m3(w[n,k]) * x[m,k]. w [N,K] u8; s [1] f32
+ * (device); x [M,K] in x_dtype; y [M,N] f32 out; 1 <= M <= 4; K a multiple of 16. */
+int dq_gemv_fp8(const uint8_t *w, const float *s, const void *x, int x_dtype, int M, int N, int K, float *y,
+                void *stream);
+
+/* Replaces `_gemv_nvfp4` / `_gemv_nvfp4_m2` (dense_q.py:56-80, :106-136):
+ * y[m, n] = s2 * sum_g e4m3(sc[n,g]) * sum_{16} e2m1(w[n,.]) * x[m,.]. w [N,K/2] u8; sc [N,K/16] e4m3;
+ * s2 [1] f32 (device); 1 <= M <= 4; K a multiple of 32. */
+int dq_gemv_nvfp4(const uint8_t *w, const uint8_t *sc, const float *s2, const void *x, int x_dtype, int M, int N,
+                  int K, float *y, void *stream);
+
+/* Replaces `dequant_rows` (dense_q.py:179-188): rows [r0, r1) (r1 <= N) of a quantized weight -> out [r1-r0, K]
+ * (FP8: e4m3 * s; NVFP4: e2m1 * (e4m3 * s2), computed in fp32 and rounded to out_dtype, a QMOE_DT_*
+ * code), bit-exact with the reference. fmt 0 = FP8, 1 = NVFP4; sc ignored for FP8. */
+int dq_dequant_rows(int fmt, const uint8_t *w, const uint8_t *sc, const float *s, int64_t N, int64_t K, int64_t r0,
+                    int64_t r1, void *out, int out_dtype, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QMOE_B200_H */

@@ -1,0 +1,250 @@
+// Quantized GEMV over "items" for sm_100a: y_item[m, n] = mult_item * sum_k W_item[n, k] * v_item[m, k].
+//
+// One kernel serves the reference's dense FP8 / NVFP4 GEMVs (dense_q.py:35-136), the orig-layout expert
+// down GEMV `_down` (qmoe_ns.py:47-67) and the per-pair prompt kernels `_up_pairs` / `_down_pairs`
+// (qmoe_ns.py:79-124). Design:
+//   - each CTA owns ROWS rows of one item; its vectors are converted once into shared memory as f16x2,
+//     scaled by an exact power of two (prescale_exp) so that every e2m1*x (NVFP4) product is exact in
+//     f16 and no f16 partial can overflow;
+//   - a warp streams whole rows with 16-byte non-allocating loads, all chunks of two rows in flight
+//     per lane; codes are decoded with the hardware e2m1x2 / e4m3x2 -> f16x2 converts and multiplied
+//     with packed HFMA2 over one 16-element group (NVFP4) or one 16-byte chunk (FP8), then each
+//     partial is widened to fp32, scaled by its block scale (NVFP4) and accumulated in fp32;
+//   - rows are reduced with warp shuffles; the item epilogue applies the fp32 multiplier (and ReLU^2).
+// The shared-memory vector layout is [m][q][chunk] of uint4 so that the 8 lanes of a quarter-warp read
+// 8 consecutive uint4 (no bank conflicts).
+#pragma once
+#include "common.cuh"
+
+namespace qmoe {
+
+enum GemvMode { GM_DENSE = 0, GM_EXPERT_DOWN = 1, GM_PAIR_UP = 2, GM_PAIR_DOWN = 3 };
+
+struct GemvArgs {
+    // dense
+    const uint8_t *w;    // [N, KB]
+    const uint8_t *sc;   // [N, K/16] (NVFP4)
+    const float *s;      // [1] device scalar (FP8 s / NVFP4 s2)
+    const void *x;       // [M, K] (dense) or [T, K] (pairs up) in x_dtype
+    int x_dtype;
+    float *y;            // output
+    int M, N, K;
+    // experts / pairs
+    const uint8_t *slots;
+    int64_t slot_bytes;
+    int64_t nslots;       // slot indices outside [0, nslots) read nothing and yield NaN
+    const int32_t *sidx;  // expert down: slot of item j; pairs: pslot
+    const int32_t *ptok;  // pairs up: token of item p (tokens outside [0, T) yield NaN)
+    int T;
+    const float *s2;      // [items, 2]
+    const float *coef;    // [items]
+    const float *hin;     // down modes: f32 vectors [items, K]
+    float *hout;          // pair up: h out [items, N]
+};
+
+constexpr int GEMV_THREADS = 256;
+constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+
+// FMT 0 = FP8 e4m3 (16 elements per 16-byte chunk), 1 = NVFP4 (32 elements per chunk, 2 scales).
+template <int FMT, int MODE, int CPL, int M>
+__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows_per_cta) {
+    constexpr int EPC = FMT == 1 ? 32 : 16;   // elements per chunk
+    constexpr int Q = EPC / 8;                // uint4 (8 f16) per chunk of the vector
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint4 *xs = reinterpret_cast<uint4 *>(smem_raw);
+    __shared__ float red[GEMV_WARPS][M];
+    __shared__ float vscale[M];
+
+    const int K = a.K;
+    const int KB = FMT == 1 ? K / 2 : K;
+    const int nch = KB / 16;   // chunks per row
+    const int item = blockIdx.y;
+    const int row0 = blockIdx.x * rows_per_cta;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- item descriptor
+    const uint8_t *W;
+    const uint8_t *S = nullptr;
+    float mult;
+    int nrows = a.N;
+    bool bad = false;
+    if (MODE == GM_DENSE) {
+        W = a.w;
+        S = a.sc;
+        mult = *a.s;
+    } else {
+        int64_t slot = a.sidx[item];
+        bad = slot < 0 || slot >= a.nslots;
+        if (MODE == GM_PAIR_UP) bad = bad || a.ptok[item] < 0 || a.ptok[item] >= a.T;
+        if (bad) slot = 0;
+        const uint8_t *blk = a.slots + slot * a.slot_bytes;
+        if (MODE == GM_PAIR_UP) {
+            W = blk + O_UW;
+            S = blk + O_US;
+            mult = a.s2[2 * item];
+        } else {
+            W = blk + O_DW;
+            S = blk + O_DS;
+            mult = a.coef[item] * a.s2[2 * item + 1];
+        }
+    }
+    if (bad) mult = __int_as_float(0x7fc00000);
+
+    // ---- vectors -> shared f16x2, prescaled by 2^E (exact)
+    // amax per vector
+    float am[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) am[m] = 0.f;
+    for (int i = tid; i < K; i += GEMV_THREADS) {
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float v;
+            if (MODE == GM_DENSE) v = load_act(a.x, a.x_dtype, (int64_t)m * K + i);
+            else if (MODE == GM_PAIR_UP) v = bad ? 0.f : load_act(a.x, a.x_dtype, (int64_t)a.ptok[item] * K + i);
+            else v = a.hin[(int64_t)item * K + i];
+            am[m] = fmaxf(am[m], fabsf(v));
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+        float v = am[m];
+        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) red[warp][m] = v;
+    }
+    __syncthreads();
+    if (tid < M) {
+        float v = 0.f;
+        for (int i = 0; i < GEMV_WARPS; ++i) v = fmaxf(v, red[i][tid]);
+        vscale[tid] = (float)prescale_exp(v, FMT == 1 ? 9 : 3);
+    }
+    __syncthreads();
+    // write xs[m][q][c]: element pair index i (elements 2i, 2i+1) -> chunk c = i / (EPC/2), q = (i % (EPC/2)) / 4
+    uint32_t *xs32 = reinterpret_cast<uint32_t *>(smem_raw);
+    for (int i = tid; i < K / 2; i += GEMV_THREADS) {
+        const int c = i / (EPC / 2), r = i % (EPC / 2), q = r / 4, wi = r % 4;
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            float v0, v1;
+            if (MODE == GM_DENSE) {
+                v0 = load_act(a.x, a.x_dtype, (int64_t)m * K + 2 * i);
+                v1 = load_act(a.x, a.x_dtype, (int64_t)m * K + 2 * i + 1);
+            } else if (MODE == GM_PAIR_UP) {
+                const int64_t b = bad ? 0 : (int64_t)a.ptok[item] * K;
+                v0 = bad ? 0.f : load_act(a.x, a.x_dtype, b + 2 * i);
+                v1 = bad ? 0.f : load_act(a.x, a.x_dtype, b + 2 * i + 1);
+            } else {
+                v0 = a.hin[(int64_t)item * K + 2 * i];
+                v1 = a.hin[(int64_t)item * K + 2 * i + 1];
+            }
+            const int E = (int)vscale[m];
+            __half2 hv = __halves2half2(__float2half_rn(ldexpf(v0, E)), __float2half_rn(ldexpf(v1, E)));
+            xs32[(((size_t)m * Q + q) * nch + c) * 4 + wi] = h2_as_u(hv);
+        }
+    }
+    __syncthreads();
+    float inv[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) inv[m] = ldexpf(1.f, -(int)vscale[m]);
+
+    // ---- rows: each warp takes rows warp, warp+8, ... two at a time
+    const int row_end = min(row0 + rows_per_cta, nrows);
+    for (int r = row0 + warp * 2; r < row_end; r += GEMV_WARPS * 2) {
+        const bool two = (r + 1) < row_end;
+        float acc[2][M];
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int m = 0; m < M; ++m) acc[rr][m] = 0.f;
+        for (int cb = 0; cb < nch; cb += 32 * CPL) {
+            uint4 wv[2][CPL];
+            uint16_t sv[2][CPL];
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr) {
+                const int row = two ? r + rr : r;
+                const uint8_t *wrow = W + (int64_t)row * KB;
+                const uint8_t *srow = FMT == 1 ? S + (int64_t)row * (K / 16) : nullptr;
+#pragma unroll
+                for (int i = 0; i < CPL; ++i) {
+                    const int c = cb + lane + 32 * i;
+                    if (c < nch) {
+                        wv[rr][i] = ldg_stream(wrow + 16 * c);
+                        if (FMT == 1) sv[rr][i] = __ldg(reinterpret_cast<const uint16_t *>(srow) + c);
+                    }
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < CPL; ++i) {
+                const int c = cb + lane + 32 * i;
+                if (c < nch) {
+#pragma unroll
+                    for (int m = 0; m < M; ++m) {
+                        uint4 xq[Q];
+#pragma unroll
+                        for (int q = 0; q < Q; ++q) xq[q] = xs[((size_t)m * Q + q) * nch + c];
+                        const uint32_t *xw = reinterpret_cast<const uint32_t *>(xq);
+#pragma unroll
+                        for (int rr = 0; rr < 2; ++rr) {
+                            const uint32_t *ww = reinterpret_cast<const uint32_t *>(&wv[rr][i]);
+                            if (FMT == 1) {
+                                __half2 g0 = __float2half2_rn(0.f), g1 = __float2half2_rn(0.f);
+                                uint32_t o[4];
+                                e2m1x8_f16x2(ww[0], o);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) g0 = __hfma2(as_h2(o[k]), as_h2(xw[k]), g0);
+                                e2m1x8_f16x2(ww[1], o);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) g0 = __hfma2(as_h2(o[k]), as_h2(xw[4 + k]), g0);
+                                e2m1x8_f16x2(ww[2], o);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) g1 = __hfma2(as_h2(o[k]), as_h2(xw[8 + k]), g1);
+                                e2m1x8_f16x2(ww[3], o);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) g1 = __hfma2(as_h2(o[k]), as_h2(xw[12 + k]), g1);
+                                const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(sv[rr][i])));
+                                acc[rr][m] = fmaf(h2sum_f32(g0), sf.x, acc[rr][m]);
+                                acc[rr][m] = fmaf(h2sum_f32(g1), sf.y, acc[rr][m]);
+                            } else {
+                                __half2 g0 = __float2half2_rn(0.f), g1 = __float2half2_rn(0.f);
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    uint32_t lo, hi;
+                                    e4m3x4_f16x2(ww[k], lo, hi);
+                                    g0 = __hfma2(as_h2(lo), as_h2(xw[2 * k]), g0);
+                                    g1 = __hfma2(as_h2(hi), as_h2(xw[2 * k + 1]), g1);
+                                }
+                                acc[rr][m] += h2sum_f32(g0) + h2sum_f32(g1);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        // warp reduction of both rows
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+            for (int m = 0; m < M; ++m)
+                for (int o = 16; o; o >>= 1) acc[rr][m] += __shfl_xor_sync(0xffffffffu, acc[rr][m], o);
+        if (lane < 2 && (lane == 0 || two)) {
+            const int row = r + lane;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const float v = (lane == 0 ? acc[0][m] : acc[1][m]) * inv[m];
+                if (MODE == GM_DENSE) {
+                    a.y[(int64_t)m * a.N + row] = v * mult;
+                } else if (MODE == GM_PAIR_UP) {
+                    float u = v * mult;
+                    u = fmaxf(u, 0.f);
+                    a.hout[(int64_t)item * a.N + row] = u * u;
+                } else {
+                    a.y[(int64_t)item * a.N + row] = v * mult;
+                }
+            }
+        }
+    }
+}
+
+// shared-memory bytes of the vector copy
+inline size_t gemv_smem_bytes(int fmt, int M, int K) { return (size_t)M * (size_t)K * 2; }
+
+} // namespace qmoe

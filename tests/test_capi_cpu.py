@@ -1,0 +1,79 @@
+"""CPU-only checks of the boundary: the library builds for sm_100a, loads, exports every function the
+header declares, the ctypes signature table covers the header exactly, and argument validation
+rejects bad calls before any CUDA work (no GPU needed for those paths)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "qmoe_b200.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return set(re.findall(r"^[A-Za-z_][\w \*]*?\b((?:qmoe|dq)_\w+)\s*\(", src, flags=re.M))
+
+
+@pytest.fixture(scope="module")
+def L():
+    import _qmoe_lib
+    if not os.path.exists(_qmoe_lib.LIB_PATH):
+        import qmoe_build
+        qmoe_build.build()
+    return _qmoe_lib
+
+
+def test_header_parse():
+    names = declared()
+    assert "qmoe_decode_groups" in names and "dq_gemv_fp8" in names
+    assert len(names) >= 15
+
+
+def test_every_declared_symbol_exported(L):
+    lib = ctypes.CDLL(L.LIB_PATH)
+    for name in sorted(declared()):
+        assert hasattr(lib, name), name
+
+
+def test_signature_table_matches_header(L):
+    assert set(L.SIGNATURES) == declared()
+
+
+def test_version_and_status_strings(L):
+    assert "sm_100a" in L.version()
+    assert L.status_string(0) == "ok"
+    assert L.status_string(4) == "device-side wait timed out"
+
+
+def test_null_and_shape_checks_need_no_gpu(L):
+    lib = L.lib()
+    assert lib.qmoe_decode_up(None, 0, 0, None, 22, None, None, 1, None, None) == 5       # NULL
+    fake = ctypes.c_void_p(16)
+    assert lib.qmoe_decode_up(fake, 1548288, 1, fake, 0, fake, fake, 1, fake, None) == 1  # K = 0
+    assert lib.qmoe_decode_up(fake, 1548290, 1, fake, 22, fake, fake, 1, fake, None) == 2  # stride not 16-aligned
+    assert lib.qmoe_decode_up(fake, 1548288, 1, fake, 22, fake, fake, 9, fake, None) == 6  # dtype
+    assert lib.dq_gemv_fp8(fake, fake, fake, 1, 5, 16, 64, fake, None) == 1                 # M > 4
+    assert lib.dq_gemv_nvfp4(fake, fake, fake, fake, 1, 1, 16, 48, fake, None) == 1         # K % 32
+    assert lib.qmoe_decode_groups_workspace_bytes(22) >= 256 + 22 * 168 * 2
+    assert lib.qmoe_decode_groups_workspace_bytes(0) == 0
+
+
+def test_no_gpu_means_device_error(L):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    lib = L.lib()
+    fake = ctypes.c_void_p(16)
+    # valid arguments, no CUDA device: the device check refuses (no fallback path exists)
+    assert lib.qmoe_decode_up(fake, 1548288, 1, fake, 22, fake, fake, 1, fake, None) == 7
+
+
+def test_python_mirror_refuses_cpu_tensors(L):
+    import torch
+    import qmoe_ns
+    blk = torch.zeros(1, qmoe_ns.BLOCK, dtype=torch.uint8)
+    with pytest.raises(L.QmoeError):
+        qmoe_ns.from_T_fast(blk, torch.zeros(qmoe_ns.LAT * qmoe_ns.KB_DN, dtype=torch.uint8))
