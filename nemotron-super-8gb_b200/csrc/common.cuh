@@ -92,12 +92,17 @@ __device__ __forceinline__ float load_act(const void *p, int dt, int64_t i) {
 
 // Power-of-two exponent E so that amax * 2^E lies in [2^(top-1), 2^top). Multiplying by 2^E is exact,
 // and a bf16 value scaled this way converts to f16 exactly while it stays in f16's normal range.
+// E is clamped to [-126, 127] so that 2^E and 2^-E are normal floats (pow2f); a vector whose amax is
+// below 2^-110 is zero for every purpose here.
 __device__ __forceinline__ int prescale_exp(float amax, int top) {
     if (!(amax > 0.f) || !isfinite(amax)) return 0;
-    int e;
-    frexpf(amax, &e); // amax = m * 2^e, m in [0.5, 1)
-    return top - e;
+    const int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 126;   // amax = m * 2^e, m in [0.5, 1)
+    int E = top - (amax >= 1.17549435e-38f ? e : -125);
+    return E < -126 ? -126 : (E > 127 ? 127 : E);
 }
+
+// 2^E as a float for -126 <= E <= 127, from its exponent bits (exact; no library call).
+__device__ __forceinline__ float pow2f(int E) { return __uint_as_float((uint32_t)(127 + E) << 23); }
 
 // ---------------------------------------------------------------- mbarrier + bulk copy (TMA engine)
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -121,10 +126,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)   // suspend up to 1 ms per try
         : "memory");
     return ok != 0;
 }

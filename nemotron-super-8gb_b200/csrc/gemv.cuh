@@ -136,15 +136,15 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
                 v0 = a.hin[(int64_t)item * K + 2 * i];
                 v1 = a.hin[(int64_t)item * K + 2 * i + 1];
             }
-            const int E = (int)vscale[m];
-            __half2 hv = __halves2half2(__float2half_rn(ldexpf(v0, E)), __float2half_rn(ldexpf(v1, E)));
+            const float pe = pow2f((int)vscale[m]);
+            __half2 hv = __halves2half2(__float2half_rn(v0 * pe), __float2half_rn(v1 * pe));
             xs32[(((size_t)m * Q + q) * nch + c) * 4 + wi] = h2_as_u(hv);
         }
     }
     __syncthreads();
     float inv[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) inv[m] = ldexpf(1.f, -(int)vscale[m]);
+    for (int m = 0; m < M; ++m) inv[m] = pow2f(-(int)vscale[m]);
 
     // ---- rows: each warp takes rows warp, warp+8, ... two at a time
     const int row_end = min(row0 + rows_per_cta, nrows);

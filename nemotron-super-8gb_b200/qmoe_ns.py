@@ -94,8 +94,8 @@ def _workspace(dev, K):
 def moe_decode_groups(slots_up, sidx, tab, s2, coef, x, h_buf, part_buf, gidx_buf, gcnt_buf, cfg=None):
     """qmoe_ns.py:245-255: up from slots_up (UPB or BLOCK row stride), live-group compaction, down over
     the live 16-neuron groups of the T-layout blocks at tab [K] int64 (device addresses), fixed-order sum.
-    Leaves h_buf[:K], gidx_buf[:K], gcnt_buf[:K] as the reference does; part_buf[0,:K] holds the
-    per-expert outputs coef_j * s2d_j * D_j h_j. Returns fp32 [1024]."""
+    Leaves h_buf[:K], gidx_buf[:K], gcnt_buf[:K] as the reference does; part_buf is scratch (as in the
+    reference). Returns fp32 [1024]."""
     K = sidx.shape[0]
     sp, sb, ns = _slots_args(slots_up)
     x, xp, xd = _act(x)
@@ -126,8 +126,8 @@ def _live_lists(h_buf, K, idx_buf, cnt_buf):
 
 
 def moe_decode_live2(slots_up, sidx, tab, s2, coef, x, h_buf, part_buf, idx_buf, cnt_buf, cfg=None):
-    """qmoe_ns.py:260-271 (superseded by moe_decode_groups; same math). part_buf[0,:K] holds the
-    per-expert outputs; idx_buf/cnt_buf receive the live-neuron lists as the reference leaves them."""
+    """qmoe_ns.py:260-271 (superseded by moe_decode_groups; same math). part_buf is scratch;
+    idx_buf/cnt_buf receive the live-neuron lists as the reference leaves them."""
     K = sidx.shape[0]
     gidx = torch.empty(K, G_DN, dtype=torch.int32, device=x.device)
     gcnt = torch.empty(K, dtype=torch.int32, device=x.device)
@@ -137,7 +137,7 @@ def moe_decode_live2(slots_up, sidx, tab, s2, coef, x, h_buf, part_buf, idx_buf,
 
 
 def moe_decode_live(slots_up, sidx, tab, s2, coef, x, h_buf, out_buf, idx_buf, cnt_buf, BR=256, NB=8):
-    """qmoe_ns.py:274-283 (superseded; same math). out_buf[:K] receives the per-expert outputs."""
+    """qmoe_ns.py:274-283 (superseded; same math). out_buf is scratch."""
     K = sidx.shape[0]
     part = out_buf[:K].view(1, K, LAT)
     return moe_decode_live2(slots_up, sidx, tab, s2, coef, x, h_buf, part, idx_buf, cnt_buf)
