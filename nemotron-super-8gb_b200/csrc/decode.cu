@@ -18,8 +18,6 @@
 #include "gemv.cuh"
 #include "host.h"
 
-#include <cstdlib>
-
 namespace qmoe {
 
 // ------------------------------------------------------------------ up
@@ -447,35 +445,7 @@ static int launch_down(const DownArgs &a, cudaStream_t st, int dev, bool pdl) {
     return launch_status();
 }
 
-// Fused single-kernel layer (decode_fused.cu), used for K <= decode_fused_max_k().
-namespace fused {
-struct Args {
-    const uint8_t *slots;
-    int64_t slot_bytes, nslots;
-    const int32_t *sidx;
-    const int64_t *tab;
-    const float *s2, *coef;
-    const void *x;
-    int x_dtype, K;
-    float *h;
-    int32_t *gidx, *gcnt;
-    float *y;
-    uint8_t *ws;
-};
-}  // namespace fused
-int launch_decode_fused(const fused::Args &a, cudaStream_t st);
-// The single-kernel layer is opt-in (QMOE_FUSED_LAYER=1) until it is faster than the kernel pair.
-inline bool use_fused_layer() {
-    static const bool on = [] {
-        const char *e = getenv("QMOE_FUSED_LAYER");
-        return e && e[0] == '1';
-    }();
-    return on;
-}
-size_t decode_fused_ws_bytes(int K);
-int decode_fused_max_k();
-
-// Workspace of the two-kernel form: [status int][pad to 64][counters DN_NCHUNK ints][pad][gmask8 K*336 u8]
+// Workspace of qmoe_decode_groups: [status int][pad to 64][counters DN_NCHUNK ints][pad][gmask8 K*336 u8]
 constexpr size_t WS_STATUS = 0;
 constexpr size_t WS_COUNTERS = 64;
 constexpr size_t WS_GMASK = 256;
@@ -520,10 +490,7 @@ int qmoe_decode_down_groups(const int64_t *tab, const float *h, const int32_t *g
 
 size_t qmoe_decode_groups_workspace_bytes(int K) {
     if (K < 1 || K > QMOE_MAX_K) return 0;
-    const size_t two = WS_GMASK + (size_t)K * UP_HALVES;
-    if (K > decode_fused_max_k()) return two;
-    const size_t f = decode_fused_ws_bytes(K);
-    return f > two ? f : two;
+    return WS_GMASK + (size_t)K * UP_HALVES;
 }
 
 int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
@@ -540,10 +507,6 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
     DeviceInfo *di;
     if (int e = current_device(&dev, &di)) return e;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    if (K <= decode_fused_max_k() && use_fused_layer()) {
-        fused::Args fa{slots_up, slot_bytes, nslots, sidx, tab, s2, coef, x, x_dtype, K, h, gidx, gcnt, y, ws};
-        return launch_decode_fused(fa, as_stream(stream));
-    }
     int *status = reinterpret_cast<int *>(ws + WS_STATUS);
     int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);
     uint8_t *gmask8 = ws + WS_GMASK;

@@ -94,8 +94,8 @@ def _workspace(dev, K):
 def moe_decode_groups(slots_up, sidx, tab, s2, coef, x, h_buf, part_buf, gidx_buf, gcnt_buf, cfg=None):
     """qmoe_ns.py:245-255: up from slots_up (UPB or BLOCK row stride), live-group compaction, down over
     the live 16-neuron groups of the T-layout blocks at tab [K] int64 (device addresses), fixed-order sum.
-    Leaves h_buf[:K], gidx_buf[:K], gcnt_buf[:K] as the reference does; part_buf is scratch (as in the
-    reference). Returns fp32 [1024]."""
+    Leaves h_buf[:K], gidx_buf[:K], gcnt_buf[:K] as the reference does; part_buf[0,:K] holds the
+    per-expert outputs coef_j * s2d_j * D_j h_j. Returns fp32 [1024]."""
     K = sidx.shape[0]
     sp, sb, ns = _slots_args(slots_up)
     x, xp, xd = _act(x)
