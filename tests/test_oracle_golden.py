@@ -101,3 +101,15 @@ def test_cpu_fp32_path_matches_fp64():
     assert np.linalg.norm(y32 - y64) / np.linalg.norm(y64) < 1e-5
     y32T = O.cpu_layer_fp32([O.to_T(b) for b in blocks], s2, coef, x, layoutT=True)
     assert np.linalg.norm(y32T - y64) / np.linalg.norm(y64) < 1e-5
+
+
+def test_router_ids_match_transformers(golden):
+    """tf:697-720 restated in qmoe_synth.route (n_group = topk_group = 1, top-22, x5.0) gives the same
+    expert ids and weights as transformers' NemotronHMoE.route_tokens_to_experts on the golden inputs."""
+    import torch
+    import qmoe_synth as S
+    h, w, b = V.route_case()
+    ids, wt = S.route(torch.from_numpy(h), torch.from_numpy(w), torch.from_numpy(b))
+    order = torch.argsort(ids, dim=1)
+    assert np.array_equal(torch.gather(ids, 1, order).numpy(), golden["route_ids"])
+    assert np.array_equal(torch.gather(wt, 1, order).numpy().view(np.uint32), golden["route_w"].view(np.uint32))
