@@ -37,6 +37,7 @@ extern "C" {
 #define QMOE_ERR_DTYPE 6       /* unknown activation dtype code */
 #define QMOE_ERR_DEVICE 7      /* the current device is not an sm_100 part */
 #define QMOE_ERR_WORKSPACE 8   /* workspace too small */
+#define QMOE_ERR_SCRATCH_LIMIT 9 /* K too large for the static scratch of qmoe_decode_groups_static */
 
 /* activation dtype codes */
 #define QMOE_DT_F32 0
@@ -94,6 +95,24 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
                        const float *s2, const float *coef, const void *x, int x_dtype, int K, float *h,
                        int32_t *gidx, int32_t *gcnt, float *part, float *y, void *workspace,
                        size_t workspace_bytes, void *stream);
+
+/* No counterpart in the reference. The decode-step layer of qmoe_decode_groups for callers that cannot call
+ * cudaMalloc: hosts whose device memory is already committed to their own fixed pool or arena (for
+ * example an engine that reserves HBM for the resident expert store and its caches up front), code running
+ * while a CUDA graph is captured in a mode where allocation calls are refused, and thin foreign-language
+ * hosts that only pass through pointers they were given. It allocates nothing: its scratch is a
+ * QMOE_STATIC_SCRATCH_BYTES array of device memory inside the library, which every GPU that loads the
+ * library holds until the process exits. Limit: K <= QMOE_STATIC_MAX_K, else QMOE_ERR_SCRATCH_LIMIT before
+ * any work. The first call on a device looks up the array's device address (once per device), so make
+ * that first call before any stream capture. All calls share the one array: calls that overlap on the GPU
+ * (other streams, other host threads) race and corrupt each other's results, so serialise them. The
+ * arrival counters that must start at zero are cleared on every call; the other contents are rewritten.
+ * Arguments and outputs as qmoe_decode_groups, without the workspace. */
+#define QMOE_STATIC_SCRATCH_BYTES 32768
+#define QMOE_STATIC_MAX_K 96
+int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
+                              const int64_t *tab, const float *s2, const float *coef, const void *x, int x_dtype,
+                              int K, float *h, int32_t *gidx, int32_t *gcnt, float *part, float *y, void *stream);
 
 /* Replaces `moe_decode` (qmoe_ns.py:70-76), the orig-layout decode forward (full down, no skip):
  * h [K,2688] f32 out, out [K,1024] f32 out (out[j] = coef[j]*s2[j,1]*D_j h_j), y [1024] = sum_j out[j]

@@ -31,6 +31,7 @@ SIGNATURES = {
     "qmoe_decode_down_groups": (_i, [_p, _p, _p, _p, _p, _p, _i, _i, _p, _p]),
     "qmoe_decode_groups_workspace_bytes": (_sz, [_i]),
     "qmoe_decode_groups": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _sz, _p]),
+    "qmoe_decode_groups_static": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p]),
     "qmoe_decode": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _i, _i, _p, _p, _p, _p]),
     "qmoe_pairs": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qmoe_from_T": (_i, [_p, _i, _p, _p]),

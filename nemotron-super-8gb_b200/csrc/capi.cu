@@ -17,6 +17,7 @@ const char *qmoe_status_string(int status) {
     case QMOE_ERR_DTYPE: return "unknown activation dtype";
     case QMOE_ERR_DEVICE: return "current device is not sm_100";
     case QMOE_ERR_WORKSPACE: return "workspace too small";
+    case QMOE_ERR_SCRATCH_LIMIT: return "K exceeds the static scratch of the allocation-free entry point";
     default: return "unknown status";
     }
 }

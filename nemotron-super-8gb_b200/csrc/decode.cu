@@ -450,6 +450,27 @@ constexpr size_t WS_STATUS = 0;
 constexpr size_t WS_COUNTERS = 64;
 constexpr size_t WS_GMASK = 256;
 
+// ------------------------------------------------------------------ allocation-free variant
+// Scratch of qmoe_decode_groups_static: a file-scope device array instead of a caller workspace. Every
+// GPU that loads this library holds it until the process exits. In host code the symbol is only a
+// stand-in for the device array, never a device address: kernels get the address looked up below.
+static __device__ __align__(256) uint8_t g_static_scratch[QMOE_STATIC_SCRATCH_BYTES];
+
+// Device address of g_static_scratch on device `dev`, looked up once per device (the caller has made
+// `dev` current). nullptr if the lookup failed.
+static uint8_t *static_scratch(int dev) {
+    static uint8_t *addr[MAX_DEVICES];
+    static cudaError_t err[MAX_DEVICES];
+    static std::once_flag once[MAX_DEVICES];
+    std::call_once(once[dev], [dev] {
+        void *p = nullptr;
+        err[dev] = cudaGetSymbolAddress(&p, g_static_scratch);
+        addr[dev] = static_cast<uint8_t *>(p);
+    });
+    return err[dev] == cudaSuccess ? addr[dev] : nullptr;
+}
+static_assert(WS_GMASK + (size_t)QMOE_STATIC_MAX_K * UP_HALVES <= QMOE_STATIC_SCRATCH_BYTES, "static scratch size");
+
 } // namespace qmoe
 
 using namespace qmoe;
@@ -595,6 +616,31 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
     if (!ensure_smem(kdn, smem_dn, dev, dn_done)) return QMOE_ERR_LAUNCH;
     kdn<<<dim3(LAT / 64, P), GEMV_THREADS, smem_dn, st>>>(d, 64);
     return launch_status();
+}
+
+// For callers that cannot allocate device memory: the decode-step layer of qmoe_decode_groups, with the
+// scratch in the library's static device array instead of a caller workspace. No allocation of any kind.
+int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
+                              const int64_t *tab, const float *s2, const float *coef, const void *x, int x_dtype,
+                              int K, float *h, int32_t *gidx, int32_t *gcnt, float *part, float *y, void *stream) {
+    if (!slots_up || !sidx || !tab || !s2 || !coef || !x || !h || !gidx || !gcnt || !part || !y) return QMOE_ERR_NULL;
+    if (K < 1 || nslots < 1) return QMOE_ERR_SHAPE;
+    if (K > QMOE_STATIC_MAX_K) return QMOE_ERR_SCRATCH_LIMIT;   // its workspace would not fit the static array
+    if (slot_bytes < UPB || (slot_bytes & 15) || !aligned16(slots_up)) return QMOE_ERR_ALIGN;
+    if (!valid_dtype(x_dtype)) return QMOE_ERR_DTYPE;
+    int dev;
+    DeviceInfo *di;
+    if (int e = current_device(&dev, &di)) return e;
+    uint8_t *ws = static_scratch(dev);
+    if (!ws) return QMOE_ERR_LAUNCH;
+    int *status = reinterpret_cast<int *>(ws + WS_STATUS);
+    int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);   // zeroed by the up kernel on every call
+    uint8_t *gmask8 = ws + WS_GMASK;                              // rewritten in full on every call
+    cudaStream_t st = as_stream(stream);
+    UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK};
+    if (int e = launch_up(ua, st, dev, *di)) return e;
+    DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
+    return launch_down<true>(da, st, dev, true);
 }
 
 } // extern "C"
