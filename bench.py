@@ -32,6 +32,9 @@ sys.path.insert(0, os.path.join(ROOT, "nemotron-super-8gb_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE decode us/token (40-layer routed-expert decode, bs=1)"
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_up_kernel launch (K = 22) from the ncu capture
+# summarised in profiles/decode_up_kernel_config1.md
+UP_TRAFFIC_NCU = 34082560 + 768
 N_LAYERS, NE, K = 40, 512, 22
 N_TOK = 64
 
@@ -44,6 +47,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "dense"])
     return ap.parse_args()
 
 
@@ -263,10 +267,80 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+DENSE_SHAPES = [("fp8", 4096, 4096), ("fp8", 12288, 4096), ("fp8", 4096, 8192), ("fp8", 131072, 4096),
+                ("nvfp4", 2688, 4096), ("nvfp4", 4096, 2688)]
+
+
+def run_dense(args):
+    """dense_q GEMVs at bs = 1 (and M = 2), FP8 per-tensor and NVFP4 weights drawn
+    N(0, 0.02) before quantization, bf16 x ~ N(0, 1). Each shape rotates over enough weight copies that the
+    bytes of one rotation exceed L2; time per call from CUDA events over graph replays."""
+    import torch
+    import dense_q as D
+    import qmoe_synth as S
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    hbm, peak_kind = peaks()
+    g = S.seeded(77, dev)
+    st = torch.cuda.Stream()
+    res = []
+    for fmt, N, K in DENSE_SHAPES:
+        wbytes = N * K if fmt == "fp8" else N * K // 2 + N * K // 16
+        copies = max(1, min(8, -(-256 * 2**20 // wbytes)))
+        qs = []
+        for c in range(copies):
+            wf = torch.randn(N, K, generator=g, device=dev) * 0.02
+            if fmt == "fp8":
+                codes, s_ = S.quantize_fp8(wf)
+                qs.append({"fmt": "fp8", "w": codes, "s": s_.reshape(1), "N": N, "K": K})
+            else:
+                codes, sc, s2 = S.quantize_nvfp4(wf)
+                qs.append({"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2.reshape(1), "N": N, "K": K})
+            del wf
+        x = torch.randn(2, K, generator=g, device=dev).to(torch.bfloat16)
+        for M in (1, 2):
+            with torch.cuda.stream(st):
+                for q in qs:
+                    D.gemv(q, x[0]) if M == 1 else D.gemv_mb(q, x[:M])
+                gr = torch.cuda.CUDAGraph()
+                reps = 4 * copies
+                with torch.cuda.graph(gr, stream=st):
+                    for r in range(reps):
+                        q = qs[r % copies]
+                        D.gemv(q, x[0]) if M == 1 else D.gemv_mb(q, x[:M])
+                for _ in range(3):
+                    gr.replay()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(10):
+                    gr.replay()
+                e1.record(st)
+                e1.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (10 * reps)
+            b = wbytes + M * K * 2 + M * N * 4
+            res.append({"fmt": fmt, "N": N, "K": K, "M": M, "us": round(us, 3), "GB/s": round(b / us / 1e3, 1),
+                        "frac": round(b / us / 1e3 / hbm, 4)})
+        del qs
+        torch.cuda.empty_cache()
+    tot_us = sum(r["us"] for r in res if r["M"] == 1)
+    tot_b = sum((r["N"] * r["K"] if r["fmt"] == "fp8" else r["N"] * r["K"] * 9 // 16) for r in res if r["M"] == 1)
+    line = {"metric": "dense_q GEMV us per call (config 2 sweep, bs=1)", "value": round(tot_us, 3), "unit": "us (sum of shapes)",
+            "n_gpus": 1, "higher_is_better": False, "dtype": "fp8/nvfp4xbf16->f32", "data": "synthetic",
+            "config": {"workload": "config2: dense_q GEMV sweep", "shapes": [list(s_) for s_ in DENSE_SHAPES],
+                       "l2": "weight copies rotated beyond L2"},
+            "roofline": {"bound": "hbm", "achieved": round(tot_b / tot_us / 1e3, 1), "peak": hbm, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(tot_b / tot_us / 1e3 / hbm, 4)},
+            "per_shape": res}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "dense":
+        return run_dense(args)
     import torch
     import torch.distributed as dist
 
@@ -423,7 +497,8 @@ def main():
             "hbm_gbs_step": round(step_gbs, 1), "hbm_frac_step": round(step_gbs / hbm, 4),
             "bytes_per_token": int(bytes_per_token),
             "roofline": {"kernel": "decode_up_kernel", "bound": "hbm", "achieved": round(up_gbs, 1), "peak": hbm,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / hbm, 4), "traffic": None,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / hbm, 4),
+                         "traffic": UP_TRAFFIC_NCU, "traffic_source": "profiles/decode_up_kernel_config1.md",
                          "bytes_per_launch": up_bytes, "us_per_launch": round(up_us, 3)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/token", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},

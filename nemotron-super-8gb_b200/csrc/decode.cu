@@ -392,13 +392,18 @@ __global__ void __launch_bounds__(DN_THREADS) decode_down_kernel(DownArgs a) {
     }
     if (bad && tid == 0) set_error(a.status, QMOE_ERR_ALIGN);
     if (tid < DN_CHUNK) a.part[(int64_t)j * LAT + row] = out;
-    // ---- 4. the last CTA of this chunk sums the K experts in slot order
-    __threadfence();
+    // ---- 4. the last CTA of this chunk sums the K experts in slot order. The CTA barrier orders every
+    // thread's part[] store before thread 0's GPU-scope fence and arrival (fences are cumulative), and
+    // the last arriver's fence before the barrier orders its readers after all arrivals.
     __syncthreads();
-    if (tid == 0) s_last = atomicAdd(&a.counters[rc], 1) == a.K - 1;
+    if (tid == 0) {
+        __threadfence();
+        const bool last = atomicAdd(&a.counters[rc], 1) == a.K - 1;
+        if (last) __threadfence();
+        s_last = last;
+    }
     __syncthreads();
     if (s_last) {
-        __threadfence();
         if (tid < DN_CHUNK) {
             float v = 0.f;
             for (int jj = 0; jj < a.K; ++jj) v += __ldcg(&a.part[(int64_t)jj * LAT + row]);
