@@ -129,6 +129,23 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
                const float *s2p, const float *coefp, const void *X, int x_dtype, int T, int P, float *h, float *out,
                void *stream);
 
+/* Replaces the prompt path of StreamExperts.forward (nem_super.py:295-348): for T tokens with top-k
+ * expert ids ids [T,topk] (values in [0, n_experts)) and routing weights [T,topk] f32,
+ *   out[t] = sum_k (in k order) weights[t,k] * s2[e,1] * D_e relu(s2[e,0] * U_e x[t])^2,  e = ids[t,k],
+ * the moe_pairs arithmetic (qmoe_ns.py:79-133) and the per-expert fp32 path (nem_super.py:342-346) as
+ * one expert-grouped GEMM on the tensor cores (tcgen05, f16 operands decoded exactly from NVFP4, fp32
+ * accumulation; h is kept as f16 with power-of-two block scales). Expert e's block is at
+ * store + e * block_stride (block_stride >= BLOCK, multiple of 16); layout_T selects the T layout of the
+ * down half (else the orig layout). s2 [n_experts, 2] f32; x [T,1024] in x_dtype (bf16 is converted
+ * exactly); out [T,1024] f32. An id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
+ * and makes that token's output NaN. 1 <= T <= 65536, 1 <= topk <= 32, 1 <= n_experts <= 1024.
+ * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts) bytes, 256-byte aligned) holds the
+ * sorted pairs and the f16 activations of every pair; its status word must start at zero. */
+size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts);
+int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
+                         const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------ layouts */
 
 /* Replaces `from_T_fast` (qmoe_ns.py:345-353, kernel `_fromT_w` :327-342): N blocks (stride BLOCK)

@@ -1,0 +1,772 @@
+// Prefill: the routed-expert forward for T tokens at once, as an expert-grouped GEMM on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in tensor memory).
+//
+// Replaces the reference's prompt path (nem_super.py:295-348): the pair path moe_pairs
+// (qmoe_ns.py:79-133, used for T <= 64) and the per-expert CPU/fp32 path (block_deq + two F.linear per
+// expert, nem_super.py:342-346), including the fixed-order combine over top-k (nem_super.py:309, :347).
+//
+// Pipeline (all on the caller's stream, nothing allocated):
+//   1. pf_hist / pf_scan / pf_place: a deterministic counting sort of the T*topk (token, k) pairs by
+//      expert. Pairs of one expert are contiguous and ordered by token; tiles of <= 256 pairs per expert.
+//   2. pf_gather: Xp[p] = f16(x[token(p)] * 2^E), with E the per-pair power of two that puts the token's
+//      amax in [2^14, 2^15): the bf16 -> f16 conversion is then exact.
+//   3. pf_gemm<UP>: per (tile, 128 up rows): D[128 rows, N pairs] = W_up (f16, decoded exactly from NVFP4
+//      by producer warps into shared memory) x Xp^T (TMA, 128B swizzle); epilogue u = D * 2^-E * s2u,
+//      h = relu(u)^2, written as f16 with one power-of-two scale per (tile, 128-row block) so the block's
+//      amax lands in [2^14, 2^15).
+//   4. pf_gemm<DOWN>: per (tile, 128 output rows): D = (W_down * 2^(S0 - S_block)) x Hs^T over K = 2688,
+//      the per-block h scales folded into the decoded weights (exact powers of two); epilogue
+//      y = D * 2^-S0 * s2d * coef -> Op[pair] fp32.
+//   5. pf_combine: out[t] = sum_k Op[pos(t, k)] in k order (deterministic, as nem_super.py:309-347).
+//
+// Every product e2m1 * e4m3 (at most 5 significant bits, magnitude in [2^-10, 2688]) is exact in f16,
+// so the only roundings are the fp32 accumulation and the f16 storage of h (relative 2^-12).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "host.h"
+
+namespace qmoe {
+namespace pf {
+
+constexpr int NT = 256;                 // pairs per tile = largest MMA N
+constexpr int BM = 128;                 // MMA M (rows of the weight tile)
+constexpr int BK = 64;                  // K per pipeline stage (4 MMAs of K = 16)
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;    // 16 KB f16
+constexpr int B_BYTES = NT * BK * 2;    // 32 KB f16
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SLAB_BYTES = 168 * 128;   // e4m3 scales of the CTA's 128 rows (down: 168 groups)
+constexpr int NPROD = 256;              // producer threads (warps 4..11)
+constexpr int THREADS = 128 + NPROD;    // warps 0..3: MMA issue (warp 0) + epilogue
+constexpr int MT_UP = INTER / BM;       // 21
+constexpr int MT_DN = LAT / BM;         // 8
+constexpr int NKT_UP = LAT / BK;        // 16
+constexpr int NKT_DN = INTER / BK;      // 42
+constexpr int PF = 4;                   // k-stages of raw weights prefetched in registers
+constexpr int CHUNK_T = 64;             // tokens per routing chunk
+constexpr int MAX_NE = 1024;
+constexpr int MAX_TOPK = 32;
+constexpr int MAX_T = 65536;
+constexpr int TMEM_COLS = 256;
+constexpr uint32_t BOX_ROWS = 16;       // TMA box: 64 f16 (128 B) x 16 rows = 2 KB
+constexpr uint32_t BOX_BYTES = BOX_ROWS * 128;
+
+// Shared memory carve-up, from a 1024-byte aligned base (the 128B swizzle repeats every 1024 bytes).
+constexpr int OFF_SLAB = STAGES * STAGE_BYTES;
+constexpr int OFF_COLSC = OFF_SLAB + SLAB_BYTES;         // 256 f32 per-column epilogue factors
+constexpr int OFF_SFAC = OFF_COLSC + NT * 4;             // 32 f16x2 per-k-block weight factors (down)
+constexpr int OFF_RED = OFF_SFAC + 32 * 4;               // 8 ints
+constexpr int OFF_BAR = OFF_RED + 32;                    // mbarriers (8-byte aligned)
+constexpr int NBAR = 2 * STAGES + 1;
+constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+constexpr int SMEM_USED = OFF_TMEM + 16;
+constexpr int SMEM_BYTES = SMEM_USED + 1024;              // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "fits the 227 KB opt-in");
+static_assert(INTER % BM == 0 && LAT % BM == 0 && LAT % BK == 0 && INTER % BK == 0, "tiling");
+
+enum { PH_UP = 0, PH_DN_T = 1, PH_DN_O = 2 };
+
+struct Params {
+    const uint8_t *store;   // expert e's block at store + e * bstride
+    int64_t bstride;
+    int ne;
+    const int32_t *ids;     // [T, topk]
+    const float *wts;       // [T, topk]
+    const float *s2;        // [ne, 2]: (up, down) weight_scale_2
+    const void *x;          // [T, 1024]
+    int x_dtype;
+    int T, topk, P, nchunks, tiles_cap;
+    float *out;             // [T, 1024] f32
+    int *status;
+    int *tile_count;
+    int *cnt;               // [ne]
+    int *eoff;              // [ne + 1]
+    int *chunk_hist;        // [nchunks, ne] counts, then per-chunk offsets
+    int4 *tiles;            // [tiles_cap] (expert, first pair, pairs, 0)
+    int *pair_tok;          // [P]
+    float *pair_coef;       // [P]
+    int *pair_pos;          // [T * topk] sorted position of (t, k), -1 if the id was invalid
+    int *pair_exp;          // [P]
+    int *tile_scale;        // [tiles_cap, 21]
+    __half *xp;             // [P, 1024]
+    __half *hs;             // [P, 2688]
+    float *op;              // [P, 1024]
+};
+
+// ------------------------------------------------------------------------------------------ routing
+// Per chunk of CHUNK_T tokens: histogram of expert ids. An id outside [0, ne) is recorded as a shape
+// error and its pair dropped (its (t, k) slot then yields NaN in the combine).
+__global__ void __launch_bounds__(256) pf_hist_kernel(const Params p) {
+    __shared__ int hist[MAX_NE];
+    for (int e = threadIdx.x; e < p.ne; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const int t0 = blockIdx.x * CHUNK_T;
+    const int t1 = min(p.T, t0 + CHUNK_T);
+    const int n = (t1 - t0) * p.topk;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int e = p.ids[(int64_t)t0 * p.topk + i];
+        if (e < 0 || e >= p.ne) {
+            set_error(p.status, QMOE_ERR_SHAPE);
+            continue;
+        }
+        atomicAdd(&hist[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < p.ne; e += blockDim.x) p.chunk_hist[(int64_t)blockIdx.x * p.ne + e] = hist[e];
+}
+
+// One CTA: per expert, the running offset of each chunk (in place), the expert's pair count and offset,
+// and the tile list (tiles of NT pairs, experts in ascending order).
+__global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
+    __shared__ int warp_sum[2][32];
+    const int e = threadIdx.x;
+    int run = 0;
+    if (e < p.ne) {
+        int c = 0;
+        for (; c + 8 <= p.nchunks; c += 8) {
+            int v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = p.chunk_hist[(int64_t)(c + i) * p.ne + e];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                p.chunk_hist[(int64_t)(c + i) * p.ne + e] = run;
+                run += v[i];
+            }
+        }
+        for (; c < p.nchunks; c++) {
+            const int v = p.chunk_hist[(int64_t)c * p.ne + e];
+            p.chunk_hist[(int64_t)c * p.ne + e] = run;
+            run += v;
+        }
+    }
+    const int cnt = run;
+    const int ntile = (cnt + NT - 1) / NT;
+    // block exclusive scans of (cnt, ntile) in thread (= expert) order
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int a = cnt, b = ntile;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= o) { a += ya; b += yb; }
+    }
+    if (lane == 31) { warp_sum[0][warp] = a; warp_sum[1][warp] = b; }
+    __syncthreads();
+    if (warp == 0) {
+        int wa = warp_sum[0][lane], wb = warp_sum[1][lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ya = __shfl_up_sync(0xffffffffu, wa, o), yb = __shfl_up_sync(0xffffffffu, wb, o);
+            if (lane >= o) { wa += ya; wb += yb; }
+        }
+        warp_sum[0][lane] = wa;
+        warp_sum[1][lane] = wb;
+    }
+    __syncthreads();
+    const int off = a - cnt + (warp ? warp_sum[0][warp - 1] : 0);
+    const int toff = b - ntile + (warp ? warp_sum[1][warp - 1] : 0);
+    if (e < p.ne) {
+        p.cnt[e] = cnt;
+        p.eoff[e] = off;
+        for (int i = 0; i < ntile; i++) {
+            const int n0 = off + i * NT;
+            p.tiles[toff + i] = make_int4(e, n0, min(NT, cnt - i * NT), 0);
+        }
+    }
+    if (threadIdx.x == blockDim.x - 1) {
+        p.eoff[p.ne] = warp_sum[0][31];
+        *p.tile_count = warp_sum[1][31];
+    }
+}
+
+// One warp per chunk: walks the chunk's tokens in order and gives each (t, k) its position inside its
+// expert's run. Equal ids inside one token (not produced by a top-k router) are ranked by k.
+__global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
+    __shared__ int base[MAX_NE];
+    __shared__ int sid[CHUNK_T * MAX_TOPK];
+    const int lane = threadIdx.x;
+    const int c = blockIdx.x;
+    for (int e = lane; e < p.ne; e += 32) base[e] = p.eoff[e] + p.chunk_hist[(int64_t)c * p.ne + e];
+    const int t0 = c * CHUNK_T;
+    const int t1 = min(p.T, t0 + CHUNK_T);
+    const int n = (t1 - t0) * p.topk;
+    for (int i = lane; i < n; i += 32) sid[i] = p.ids[(int64_t)t0 * p.topk + i];
+    __syncwarp();
+    const uint32_t lt = (1u << lane) - 1u;
+    for (int t = t0; t < t1; t++) {
+        const bool valid = lane < p.topk;
+        const int e = valid ? sid[(t - t0) * p.topk + lane] : -1;
+        const bool ok = valid && e >= 0 && e < p.ne;
+        const uint32_t mask = __match_any_sync(0xffffffffu, ok ? e : -1 - lane);
+        const int64_t tk = (int64_t)t * p.topk + lane;
+        if (ok) {
+            const int pos = base[e] + __popc(mask & lt);
+            p.pair_tok[pos] = t;
+            p.pair_coef[pos] = p.wts[tk];
+            p.pair_pos[tk] = pos;
+        } else if (valid) {
+            p.pair_pos[tk] = -1;
+        }
+        __syncwarp();
+        if (ok && (mask & lt) == 0) base[e] += __popc(mask);
+        __syncwarp();
+    }
+}
+
+// One warp per sorted pair: Xp[p] = f16(x[t] * 2^E), E from the token's amax (exact for bf16 input).
+__global__ void __launch_bounds__(256) pf_gather_kernel(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pr >= p.eoff[p.ne]) return;
+    const int t = p.pair_tok[pr];
+    float v[32];
+    if (p.x_dtype == QMOE_DT_BF16) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) +
+                                                          (int64_t)t * LAT + lane * 32);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 w = src[i];
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                v[i * 8 + 2 * j] = __uint_as_float(u[j] << 16);
+                v[i * 8 + 2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = load_act(p.x, p.x_dtype, (int64_t)t * LAT + lane * 32 + i);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const int E = prescale_exp(amax, 15);
+    const float sc = pow2f(E);
+    uint32_t o[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[i] = h2_as_u(__floats2half2_rn(v[2 * i] * sc, v[2 * i + 1] * sc));
+    uint4 *dst = reinterpret_cast<uint4 *>(p.xp + (int64_t)pr * LAT + lane * 32);
+#pragma unroll
+    for (int i = 0; i < 4; i++) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    if (lane == 0) p.pair_exp[pr] = E;
+}
+
+// out[t] = sum over k (in order) of Op[pos(t, k)]; an invalid (t, k) contributes NaN.
+__global__ void __launch_bounds__(256) pf_combine_kernel(const Params p) {
+    const int t = blockIdx.x;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < p.topk; k++) {
+        const int pos = p.pair_pos[(int64_t)t * p.topk + k];
+        float4 v;
+        if (pos >= 0) {
+            v = reinterpret_cast<const float4 *>(p.op + (int64_t)pos * LAT)[threadIdx.x];
+        } else {
+            const float nan = __int_as_float(0x7fc00000);
+            v = make_float4(nan, nan, nan, nan);
+        }
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    reinterpret_cast<float4 *>(p.out + (int64_t)t * LAT)[threadIdx.x] = acc;
+}
+
+// ------------------------------------------------------------------------------------------ tcgen05
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("barrier.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Shared-memory matrix descriptor (tcgen05 "matrix descriptor", version 1): start, leading and stride
+// byte offsets in 16-byte units, layout type in bits 61-63 (0 = no swizzle, 2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
+}
+
+// Instruction descriptor of kind::f16: f32 accumulator, A and B f16, B K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t instr_desc_f16(int n, bool a_mn_major) {
+    return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 32 lanes x 32 consecutive f32 columns of tensor memory -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// 2-D tiled TMA load of one box into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// 2^d as f16x2 for d <= 0 (exact while 2^d >= 2^-24, zero below).
+__device__ __forceinline__ uint32_t pow2_h2(int d) {
+    uint32_t h;
+    if (d >= -14) h = (uint32_t)(15 + d) << 10;
+    else if (d >= -24) h = 1u << (d + 24);
+    else h = 0u;
+    return h | (h << 16);
+}
+
+// Raw weight bytes of one k-stage for this producer thread (16 bytes).
+template <int PH>
+__device__ __forceinline__ uint4 load_raw(const uint8_t *blk, int mt, int kt, int pt) {
+    const uint8_t *src;
+    if (PH == PH_UP) src = blk + O_UW + (int64_t)(mt * BM + (pt >> 1)) * KB_UP + kt * 32 + (pt & 1) * 16;
+    else if (PH == PH_DN_O) src = blk + O_DW + (int64_t)(mt * BM + (pt >> 1)) * KB_DN + kt * 32 + (pt & 1) * 16;
+    else src = blk + O_DW + (int64_t)(kt * BK + (pt >> 2)) * (LAT / 2) + mt * (BM / 2) + (pt & 3) * 16;
+    return ldg_stream(src);
+}
+
+// Decodes one k-stage of this thread's raw bytes into the A tile (f16, exact).
+//   K-major (up, down orig): thread = (row m = pt/2, half hf = pt%2): 32 codes along k, 2 scale groups;
+//     chunk c (8 k) of row m at (m/8)*1024 + c*128 + (m%8)*16 (no swizzle; LBO 128, SBO 1024).
+//   MN-major (down T layout): thread = (k = pt/4, quarter q = pt%4): 32 rows at one k, per-row scales;
+//     rows 8j..8j+7 at k at j*1024 + (k/8)*128 + (k%8)*16 (no swizzle; LBO 128 along k, SBO 1024 along m).
+template <int PH>
+__device__ __forceinline__ void decode_stage(uint32_t a_base, const uint8_t *slab, int kt, int pt, uint4 raw,
+                                             uint32_t fac) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    if (PH == PH_UP || PH == PH_DN_O) {
+        constexpr int GP = PH == PH_UP ? G_UP : G_DN;
+        const int m = pt >> 1, hf = pt & 1;
+        const uint16_t s01 = *reinterpret_cast<const uint16_t *>(slab + m * GP + kt * 4 + hf * 2);
+        __half2 sc = as_h2(e4m3x2_f16x2(s01));
+        if (PH == PH_DN_O) sc = __hmul2(sc, as_h2(fac));
+        const __half2 sa = __low2half2(sc), sb = __high2half2(sc);
+        const uint32_t row = a_base + (m >> 3) * 1024 + (m & 7) * 16;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            uint32_t o[4];
+            e2m1x8_f16x2(w[i], o);
+            const __half2 s = i < 2 ? sa : sb;
+            st_shared_v4(row + (hf * 4 + i) * 128, h2_as_u(__hmul2(as_h2(o[0]), s)), h2_as_u(__hmul2(as_h2(o[1]), s)),
+                         h2_as_u(__hmul2(as_h2(o[2]), s)), h2_as_u(__hmul2(as_h2(o[3]), s)));
+        }
+    } else {
+        const int kl = pt >> 2, q = pt & 3;
+        const int g = (kt * BK + kl) >> 4;
+        const uint8_t *srow = slab + g * BM + q * 32;
+        const uint32_t kaddr = a_base + (kl >> 3) * 128 + (kl & 7) * 16;
+        const __half2 f = as_h2(fac);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint2 s8 = *reinterpret_cast<const uint2 *>(srow + i * 8);
+            uint32_t s[4];
+            e4m3x4_f16x2(s8.x, s[0], s[1]);
+            e4m3x4_f16x2(s8.y, s[2], s[3]);
+            uint32_t o[4];
+            e2m1x8_f16x2(w[i], o);
+            st_shared_v4(kaddr + (q * 4 + i) * 1024, h2_as_u(__hmul2(as_h2(o[0]), __hmul2(as_h2(s[0]), f))),
+                         h2_as_u(__hmul2(as_h2(o[1]), __hmul2(as_h2(s[1]), f))),
+                         h2_as_u(__hmul2(as_h2(o[2]), __hmul2(as_h2(s[2]), f))),
+                         h2_as_u(__hmul2(as_h2(o[3]), __hmul2(as_h2(s[3]), f))));
+        }
+    }
+}
+
+// Smallest h-block scale exponent of a tile (the block with the largest amax) over its 21 up blocks,
+// reduced across one warp; lane l < 21 also returns its own block's exponent in *mine.
+__device__ __forceinline__ int tile_s0(const Params &p, int tile, int lane, int *mine) {
+    const int s = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
+    int m = s;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+    *mine = s;
+    return m;
+}
+
+// The grouped GEMM. grid = (row blocks, tile capacity); CTAs past the tile count exit at once.
+template <int PH>
+__global__ void __launch_bounds__(THREADS, 1) pf_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tmb) {
+    constexpr int NKT = PH == PH_UP ? NKT_UP : NKT_DN;
+    const int mt = blockIdx.x;
+    const int tile = blockIdx.y;
+    if (tile >= *p.tile_count) return;
+    const int4 td = p.tiles[tile];
+    const int e = td.x, n0 = td.y, n = td.z;
+    const int N = (n + 15) & ~15;
+    const uint8_t *blk = p.store + (int64_t)e * p.bstride;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    uint8_t *sm = smem_raw + (((raw_base + 1023u) & ~1023u) - raw_base);
+    const uint32_t sbase = smem_u32(sm);
+    uint8_t *slab = sm + OFF_SLAB;
+    float *colsc = reinterpret_cast<float *>(sm + OFF_COLSC);
+    uint32_t *sfac = reinterpret_cast<uint32_t *>(sm + OFF_SFAC);
+    float *red = reinterpret_cast<float *>(sm + OFF_RED);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
+    uint64_t *empty = full + STAGES;
+    uint64_t *accb = empty + STAGES;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], NPROD + 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accb, 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= 4) {
+        // ------------------------------------------------------------------ producers
+        const int pt = tid - 128;
+        if (PH == PH_UP) {
+            const uint8_t *src = blk + O_US + (int64_t)mt * BM * G_UP;
+            for (int i = pt; i < BM * G_UP / 16; i += NPROD)
+                reinterpret_cast<uint4 *>(slab)[i] = ldg_stream(src + i * 16);
+        } else if (PH == PH_DN_O) {
+            const uint8_t *src = blk + O_DS + (int64_t)mt * BM * G_DN;
+            for (int i = pt; i < BM * G_DN / 16; i += NPROD)
+                reinterpret_cast<uint4 *>(slab)[i] = ldg_stream(src + i * 16);
+        } else {
+            for (int i = pt; i < G_DN * (BM / 16); i += NPROD) {
+                const int g = i >> 3, q = i & 7;
+                reinterpret_cast<uint4 *>(slab + g * BM)[q] = ldg_stream(blk + O_DS + (int64_t)g * LAT + mt * BM + q * 16);
+            }
+        }
+        if (PH != PH_UP && warp == 4) {
+            int mine;
+            const int s0 = tile_s0(p, tile, lane, &mine);
+            if (lane < MT_UP) sfac[lane] = pow2_h2(s0 - mine);
+        }
+        named_sync(1, NPROD);
+
+        uint4 pre[PF];
+#pragma unroll
+        for (int i = 0; i < PF; i++) pre[i] = load_raw<PH>(blk, mt, i, pt);
+        bool ok = true;
+        for (int kt0 = 0; kt0 < NKT && ok; kt0 += PF) {
+#pragma unroll
+            for (int i = 0; i < PF; i++) {
+                const int kt = kt0 + i;
+                if (kt >= NKT) break;
+                const uint4 cur = pre[i];
+                if (kt + PF < NKT) pre[i] = load_raw<PH>(blk, mt, kt + PF, pt);
+                const int s = kt % STAGES;
+                const uint32_t use = kt / STAGES;
+                if (!mbar_wait(&empty[s], (use & 1u) ^ 1u)) {
+                    set_error(p.status, DEV_ERR_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                uint8_t *a_tile = sm + s * STAGE_BYTES;
+                if (pt == 0) {
+                    mbar_expect_tx(&full[s], (uint32_t)(N / 16) * BOX_BYTES);
+                    for (int b = 0; b < N / 16; b++)
+                        tma_load_2d(a_tile + A_BYTES + b * BOX_BYTES, &tmb, kt * BK, n0 + b * 16, &full[s]);
+                }
+                decode_stage<PH>(sbase + s * STAGE_BYTES, slab, kt, pt, cur, PH == PH_UP ? 0u : sfac[kt >> 1]);
+                fence_async_smem();
+                mbar_arrive(&full[s]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ MMA issue (warp 0) + epilogue
+        if (warp == 0) {
+            const uint32_t idesc = instr_desc_f16(N, PH == PH_DN_T);
+            bool ok = true;
+            for (int kt = 0; kt < NKT; kt++) {
+                const int s = kt % STAGES;
+                const uint32_t use = kt / STAGES;
+                if (lane == 0) ok = mbar_wait(&full[s], use & 1u);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    if (lane == 0) set_error(p.status, DEV_ERR_TIMEOUT);
+                    break;
+                }
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t a0 = sbase + s * STAGE_BYTES;
+                    const uint32_t b0 = a0 + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++) {
+                        const uint64_t ad = smem_desc(a0 + k * 256, 128, 1024, 0);
+                        const uint64_t bd = smem_desc(b0 + k * 32, 16, 1024, 2);
+                        mma_f16(tmem, ad, bd, idesc, (kt | k) != 0);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) mma_commit(accb);   // also after a failed wait: tracks every MMA issued
+            __syncwarp();
+        }
+        // per-column factors
+        int s0 = 0;
+        if (PH != PH_UP) {
+            int mine;
+            s0 = tile_s0(p, tile, lane, &mine);
+        }
+        for (int j = tid; j < n; j += 128) {
+            if (PH == PH_UP) colsc[j] = pow2f(-p.pair_exp[n0 + j]) * p.s2[(int64_t)e * 2];
+            else colsc[j] = p.pair_coef[n0 + j] * p.s2[(int64_t)e * 2 + 1] * pow2f(-s0);
+        }
+        named_sync(2, 128);
+        const bool acc_ok = mbar_wait(accb, 0);
+        if (!acc_ok && tid == 0) set_error(p.status, DEV_ERR_TIMEOUT);
+        tc_fence_after();
+        const int m = tid;   // accumulator row = TMEM lane
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        if (PH == PH_UP) {
+            // pass 1: amax of h over the 128 x n block (every thread reaches the same barriers)
+            float mx = 0.f;
+            if (acc_ok) {
+                for (int c0 = 0; c0 < n; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(trow + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (c0 + j < n) {
+                            const float u = v[j] * colsc[c0 + j];
+                            mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            if (lane == 0) red[warp] = mx;
+            named_sync(2, 128);
+            mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+            // an all-zero block takes the largest exponent so that it never sets the tile's reference
+            const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
+            if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
+            // pass 2: h * 2^S as f16 (the block's amax lands in [2^14, 2^15))
+            if (acc_ok) {
+                const float sc = pow2f(S);
+                __half *dst = p.hs + (int64_t)n0 * INTER + mt * BM + m;
+                for (int c0 = 0; c0 < n; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(trow + c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        if (c0 + j < n) {
+                            const float u = v[j] * colsc[c0 + j];
+                            dst[(int64_t)(c0 + j) * INTER] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
+                        }
+                    }
+                }
+            }
+        } else if (acc_ok) {
+            float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
+            for (int c0 = 0; c0 < n; c0 += 32) {
+                float v[32];
+                tmem_ld32(trow + c0, v);
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    if (c0 + j < n) dst[(int64_t)(c0 + j) * LAT] = v[j] * colsc[c0 + j];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------------------------------ host
+struct WsLayout {
+    size_t status, tile_count, cnt, eoff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
+        xp, hs, op, total;
+    int P, nchunks, tiles_cap;
+};
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline WsLayout ws_layout(int T, int topk, int ne) {
+    WsLayout L{};
+    L.P = T * topk;
+    L.nchunks = (T + CHUNK_T - 1) / CHUNK_T;
+    L.tiles_cap = (L.P + NT - 1) / NT + (ne < L.P ? ne : L.P);
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes, 256);
+        return at;
+    };
+    L.status = take(64);
+    L.tile_count = take(4);
+    L.cnt = take(sizeof(int) * ne);
+    L.eoff = take(sizeof(int) * (ne + 1));
+    L.chunk_hist = take(sizeof(int) * (size_t)L.nchunks * ne);
+    L.tiles = take(sizeof(int4) * (size_t)L.tiles_cap);
+    L.pair_tok = take(sizeof(int) * (size_t)L.P);
+    L.pair_coef = take(sizeof(float) * (size_t)L.P);
+    L.pair_pos = take(sizeof(int) * (size_t)L.P);
+    L.pair_exp = take(sizeof(int) * (size_t)L.P);
+    L.tile_scale = take(sizeof(int) * (size_t)L.tiles_cap * MT_UP);
+    L.xp = take((size_t)L.P * LAT * 2);
+    L.hs = take((size_t)L.P * INTER * 2);
+    L.op = take((size_t)L.P * LAT * 4);
+    L.total = o;
+    return L;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    });
+    return fn;
+}
+
+// Row-major f16 matrix [rows, cols] -> map with 64 x 16 boxes and 128-byte swizzle.
+inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {BK, BOX_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+std::atomic<uint64_t> g_smem_up{0}, g_smem_dn_t{0}, g_smem_dn_o{0};
+
+} // namespace pf
+} // namespace qmoe
+
+using namespace qmoe;
+
+extern "C" {
+
+size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts) {
+    if (T < 1 || T > pf::MAX_T || topk < 1 || topk > pf::MAX_TOPK || n_experts < 1 || n_experts > pf::MAX_NE) return 0;
+    return pf::ws_layout(T, topk, n_experts).total;
+}
+
+int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
+                         const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
+                         void *workspace, size_t workspace_bytes, void *stream) {
+    using namespace qmoe::pf;
+    if (!store || !ids || !weights || !s2 || !x || !out || !workspace) return QMOE_ERR_NULL;
+    if (T < 1 || T > MAX_T || topk < 1 || topk > MAX_TOPK || n_experts < 1 || n_experts > MAX_NE)
+        return QMOE_ERR_SHAPE;
+    if (block_stride < BLOCK) return QMOE_ERR_SHAPE;
+    if (!valid_dtype(x_dtype)) return QMOE_ERR_DTYPE;
+    if ((block_stride & 15) || !aligned16(store) || !aligned16(x) || !aligned16(out) || !aligned4(ids) ||
+        !aligned4(weights) || !aligned4(s2) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
+        return QMOE_ERR_ALIGN;
+    const WsLayout L = ws_layout(T, topk, n_experts);
+    if (workspace_bytes < L.total) return QMOE_ERR_WORKSPACE;
+    int dev;
+    DeviceInfo *di;
+    if (int rc = current_device(&dev, &di)) return rc;
+    (void)di;
+
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    Params p{};
+    p.store = store;
+    p.bstride = block_stride;
+    p.ne = n_experts;
+    p.ids = ids;
+    p.wts = weights;
+    p.s2 = s2;
+    p.x = x;
+    p.x_dtype = x_dtype;
+    p.T = T;
+    p.topk = topk;
+    p.P = L.P;
+    p.nchunks = L.nchunks;
+    p.tiles_cap = L.tiles_cap;
+    p.out = out;
+    p.status = reinterpret_cast<int *>(ws + L.status);
+    p.tile_count = reinterpret_cast<int *>(ws + L.tile_count);
+    p.cnt = reinterpret_cast<int *>(ws + L.cnt);
+    p.eoff = reinterpret_cast<int *>(ws + L.eoff);
+    p.chunk_hist = reinterpret_cast<int *>(ws + L.chunk_hist);
+    p.tiles = reinterpret_cast<int4 *>(ws + L.tiles);
+    p.pair_tok = reinterpret_cast<int *>(ws + L.pair_tok);
+    p.pair_coef = reinterpret_cast<float *>(ws + L.pair_coef);
+    p.pair_pos = reinterpret_cast<int *>(ws + L.pair_pos);
+    p.pair_exp = reinterpret_cast<int *>(ws + L.pair_exp);
+    p.tile_scale = reinterpret_cast<int *>(ws + L.tile_scale);
+    p.xp = reinterpret_cast<__half *>(ws + L.xp);
+    p.hs = reinterpret_cast<__half *>(ws + L.hs);
+    p.op = reinterpret_cast<float *>(ws + L.op);
+
+    CUtensorMap map_x, map_h;
+    if (!make_map(&map_x, p.xp, L.P, LAT) || !make_map(&map_h, p.hs, L.P, INTER)) return QMOE_ERR_LAUNCH;
+
+    auto up = pf_gemm_kernel<PH_UP>;
+    auto dn = layout_T ? pf_gemm_kernel<PH_DN_T> : pf_gemm_kernel<PH_DN_O>;
+    if (!ensure_smem(up, SMEM_BYTES, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
+    if (!ensure_smem(dn, SMEM_BYTES, dev, layout_T ? g_smem_dn_t : g_smem_dn_o)) return QMOE_ERR_LAUNCH;
+
+    cudaStream_t st = as_stream(stream);
+    pf_hist_kernel<<<L.nchunks, 256, 0, st>>>(p);
+    pf_scan_kernel<<<1, 1024, 0, st>>>(p);
+    pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
+    pf_gather_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
+    up<<<dim3(MT_UP, L.tiles_cap), THREADS, SMEM_BYTES, st>>>(p, map_x);
+    dn<<<dim3(MT_DN, L.tiles_cap), THREADS, SMEM_BYTES, st>>>(p, map_h);
+    pf_combine_kernel<<<T, 256, 0, st>>>(p);
+    return launch_status();
+}
+
+} // extern "C"

@@ -143,6 +143,56 @@ def moe_decode_live(slots_up, sidx, tab, s2, coef, x, h_buf, out_buf, idx_buf, c
     return moe_decode_live2(slots_up, sidx, tab, s2, coef, x, h_buf, part, idx_buf, cnt_buf)
 
 
+_PWS = {}
+
+
+def _prefill_workspace(dev, T, topk, ne):
+    """Per (device, stream) workspace of qmoe_prefill_grouped, grown on demand; status word zeroed."""
+    key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
+    need = int(C.lib().qmoe_prefill_workspace_bytes(T, topk, ne))
+    if need == 0:
+        raise C.QmoeError(f"prefill shape out of range: T={T} topk={topk} n_experts={ne}")
+    ws = _PWS.get(key)
+    if ws is None or ws.numel() < need:
+        _PWS.pop(key, None)
+        ws = torch.empty(need + (need >> 3), dtype=torch.uint8, device=dev)
+        ws[:256].zero_()
+        _PWS[key] = ws
+    return ws
+
+
+def moe_prefill(store, ids, weights, s2, X, layout_T=True, out=None):
+    """Prompt-path routed-expert forward (nem_super.py:295-348 as one call): X [T,1024], ids [T,topk]
+    expert ids into store [E, >= BLOCK] u8 (one block per row), weights [T,topk], s2 [E,2] f32 ->
+    fp32 [T,1024] = sum over k, in k order, of weights[t,k] * expert_{ids[t,k]}(X[t]).
+    Expert-grouped GEMM on the tensor cores; layout_T: the down halves are in the T layout."""
+    if store.dtype != torch.uint8 or store.dim() != 2 or store.stride(1) != 1 or store.shape[1] < BLOCK:
+        raise C.QmoeError("store must be a uint8 [E, >= BLOCK] tensor with contiguous rows")
+    T, topk = ids.shape
+    X, xp, xd = _act(X)
+    if X.shape != (T, LAT):
+        raise C.QmoeError("X must be [T, 1024] with T = ids.shape[0]")
+    ids32 = ids.to(torch.int32).contiguous()
+    w32 = weights.to(torch.float32).contiguous()
+    s2c = s2.to(torch.float32).contiguous()
+    if out is None:
+        out = torch.empty(T, LAT, dtype=torch.float32, device=X.device)
+    ws = _prefill_workspace(X.device, T, topk, store.shape[0])
+    C.call("qmoe_prefill_grouped", C.ptr(store), int(store.stride(0)), int(store.shape[0]), int(bool(layout_T)),
+           C.ptr(ids32), C.ptr(w32), C.ptr(s2c), xp, xd, T, topk, _f32(out), C.ptr(ws), ws.numel(),
+           C.stream_of(X))
+    return out
+
+
+def prefill_status(device=None, clear=True):
+    """Device-side status of the prefill workspace on the current stream (synchronises it)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    ws = _PWS.get((dev.index, torch.cuda.current_stream(dev).cuda_stream))
+    if ws is None:
+        return 0
+    return int(C.lib().qmoe_workspace_status(C.ptr(ws), int(clear), C.stream_of(ws)))
+
+
 def moe_pairs_T(slots_u8, pslot, ptok, s2p, coefp, X, h_buf, out_buf):
     """qmoe_ns.py:318-324: pairs over T-layout slots. The slots used are converted to the orig layout
     in a scratch copy (from_T) and the pairs kernels run on it, as the reference engine's prompt path
