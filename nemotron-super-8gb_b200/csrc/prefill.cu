@@ -29,41 +29,54 @@
 namespace qmoe {
 namespace pf {
 
-constexpr int NT = 256;                 // pairs per tile = largest MMA N
+constexpr int NT = 128;                 // pairs per tile = largest MMA N used
 constexpr int BM = 128;                 // MMA M (rows of the weight tile)
-constexpr int BK = 64;                  // K per pipeline stage (4 MMAs of K = 16)
-constexpr int STAGES = 4;
+constexpr int BK = 64;                  // K per A/B stage (4 MMAs of K = 16)
+constexpr int RK = 128;                 // K per raw-weight stage: one 8 KB TMA box
+constexpr int KPR = RK / BK;            // A stages filled from one raw stage
+constexpr int SA = 4, SB = 4, SR = 6;   // ring depths: A (decoded weights), B (activations), raw weights
 constexpr int A_BYTES = BM * BK * 2;    // 16 KB f16
-constexpr int B_BYTES = NT * BK * 2;    // 32 KB f16
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SLAB_BYTES = 168 * 128;   // e4m3 scales of the CTA's 128 rows (down: 168 groups)
-constexpr int NPROD = 256;              // producer threads (warps 4..11)
-constexpr int THREADS = 128 + NPROD;    // warps 0..3: MMA issue (warp 0) + epilogue
+constexpr int B_BYTES = NT * BK * 2;    // 16 KB f16
+constexpr int RAW_BYTES = BM * RK / 2;  // 8 KB of e2m1 codes
+constexpr int SLAB_BYTES = 128 * 168;   // e4m3 scales of one item (largest: down, 168 groups x 128 rows)
+constexpr int STG_COLS = 16;            // epilogue staging: 16 pairs x 128 rows of f16
+constexpr int NDEC = 256;               // decoder threads (warps 4..11)
+constexpr int W_RAW = 12, W_B = 13, W_MMA = 14;
+constexpr int THREADS = 15 * 32;        // warps 0..3 epilogue, 4..11 decoders, 12 raw TMA, 13 B TMA, 14 MMA
 constexpr int MT_UP = INTER / BM;       // 21
 constexpr int MT_DN = LAT / BM;         // 8
 constexpr int NKT_UP = LAT / BK;        // 16
 constexpr int NKT_DN = INTER / BK;      // 42
-constexpr int PF = 4;                   // k-stages of raw weights prefetched in registers
 constexpr int CHUNK_T = 64;             // tokens per routing chunk
 constexpr int MAX_NE = 1024;
 constexpr int MAX_TOPK = 32;
 constexpr int MAX_T = 65536;
-constexpr int TMEM_COLS = 256;
-constexpr uint32_t BOX_ROWS = 16;       // TMA box: 64 f16 (128 B) x 16 rows = 2 KB
-constexpr uint32_t BOX_BYTES = BOX_ROWS * 128;
+constexpr int TMEM_COLS = 2 * NT;       // two accumulators: the epilogue of one item overlaps the next
+// Row offsets of the block regions in the TMA views of the store (row pitch 512, 1024, 1344 bytes).
+constexpr int ROW512_DNT = (int)(O_DW / 512);     // 3024: dnT_w
+constexpr int ROW1024_DNT_S = (int)(O_DS / 1024); // 2856: dnT_s
+constexpr int ROW1344_DW = (int)(O_DW / 1344);    // 1152: dn_w
+static_assert(O_DW % 512 == 0 && O_DS % 1024 == 0 && O_DW % 1344 == 0 && BLOCK % 1344 == 0, "block regions on view rows");
 
 // Shared memory carve-up, from a 1024-byte aligned base (the 128B swizzle repeats every 1024 bytes).
-constexpr int OFF_SLAB = STAGES * STAGE_BYTES;
-constexpr int OFF_COLSC = OFF_SLAB + SLAB_BYTES;         // 256 f32 per-column epilogue factors
-constexpr int OFF_SFAC = OFF_COLSC + NT * 4;             // 32 f16x2 per-k-block weight factors (down)
-constexpr int OFF_RED = OFF_SFAC + 32 * 4;               // 8 ints
-constexpr int OFF_BAR = OFF_RED + 32;                    // mbarriers (8-byte aligned)
-constexpr int NBAR = 2 * STAGES + 1;
+constexpr int OFF_A = 0;
+constexpr int OFF_B = OFF_A + SA * A_BYTES;
+constexpr int OFF_RAW = OFF_B + SB * B_BYTES;
+constexpr int OFF_SLAB = OFF_RAW + SR * RAW_BYTES;         // two item scale buffers
+constexpr int OFF_STG = OFF_SLAB + 2 * SLAB_BYTES;
+constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;     // 2 x NT f32 per-column epilogue factors
+constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;            // 2 x 4 f32 block-amax partials
+constexpr int OFF_BAR = OFF_RED + 32;
+constexpr int NBAR = 2 * SA + 2 * SB + 2 * SR + 8;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-constexpr int SMEM_USED = OFF_TMEM + 16;
-constexpr int SMEM_BYTES = SMEM_USED + 1024;              // + alignment slack
+constexpr int OFF_ABORT = OFF_TMEM + 16;
+constexpr int SMEM_USED = OFF_ABORT + 16;
+constexpr int SMEM_BYTES = SMEM_USED + 1024;               // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "fits the 227 KB opt-in");
-static_assert(INTER % BM == 0 && LAT % BM == 0 && LAT % BK == 0 && INTER % BK == 0, "tiling");
+static_assert(OFF_RAW % 1024 == 0 && OFF_B % 1024 == 0 && OFF_SLAB % 16 == 0, "TMA destinations");
+static_assert(LAT % RK == 0 && INTER % RK == 0 && INTER % BM == 0 && LAT % BM == 0, "tiling");
+constexpr int UNITS = BM * RK / 2 / 16 / NDEC;   // 16-byte raw chunks per decoder thread and stage
+constexpr int PPR = RK / 32;                     // 16-byte parts per K-major row of a raw stage
 
 enum { PH_UP = 0, PH_DN_T = 1, PH_DN_O = 2 };
 
@@ -184,13 +197,17 @@ __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
 __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
     __shared__ int base[MAX_NE];
     __shared__ int sid[CHUNK_T * MAX_TOPK];
+    __shared__ float swt[CHUNK_T * MAX_TOPK];
     const int lane = threadIdx.x;
     const int c = blockIdx.x;
     for (int e = lane; e < p.ne; e += 32) base[e] = p.eoff[e] + p.chunk_hist[(int64_t)c * p.ne + e];
     const int t0 = c * CHUNK_T;
     const int t1 = min(p.T, t0 + CHUNK_T);
     const int n = (t1 - t0) * p.topk;
-    for (int i = lane; i < n; i += 32) sid[i] = p.ids[(int64_t)t0 * p.topk + i];
+    for (int i = lane; i < n; i += 32) {
+        sid[i] = p.ids[(int64_t)t0 * p.topk + i];
+        swt[i] = p.wts[(int64_t)t0 * p.topk + i];
+    }
     __syncwarp();
     const uint32_t lt = (1u << lane) - 1u;
     for (int t = t0; t < t1; t++) {
@@ -202,7 +219,7 @@ __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
         if (ok) {
             const int pos = base[e] + __popc(mask & lt);
             p.pair_tok[pos] = t;
-            p.pair_coef[pos] = p.wts[tk];
+            p.pair_coef[pos] = swt[(t - t0) * p.topk + lane];
             p.pair_pos[tk] = pos;
         } else if (valid) {
             p.pair_pos[tk] = -1;
@@ -346,109 +363,162 @@ __device__ __forceinline__ uint32_t pow2_h2(int d) {
     return h | (h << 16);
 }
 
-// Raw weight bytes of one k-stage for this producer thread (16 bytes).
-template <int PH>
-__device__ __forceinline__ uint4 load_raw(const uint8_t *blk, int mt, int kt, int pt) {
-    const uint8_t *src;
-    if (PH == PH_UP) src = blk + O_UW + (int64_t)(mt * BM + (pt >> 1)) * KB_UP + kt * 32 + (pt & 1) * 16;
-    else if (PH == PH_DN_O) src = blk + O_DW + (int64_t)(mt * BM + (pt >> 1)) * KB_DN + kt * 32 + (pt & 1) * 16;
-    else src = blk + O_DW + (int64_t)(kt * BK + (pt >> 2)) * (LAT / 2) + mt * (BM / 2) + (pt & 3) * 16;
-    return ldg_stream(src);
+// 3-D tiled TMA load (box {x, y, 1}) into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
 }
 
-// Decodes one k-stage of this thread's raw bytes into the A tile (f16, exact).
-//   K-major (up, down orig): thread = (row m = pt/2, half hf = pt%2): 32 codes along k, 2 scale groups;
-//     chunk c (8 k) of row m at (m/8)*1024 + c*128 + (m%8)*16 (no swizzle; LBO 128, SBO 1024).
-//   MN-major (down T layout): thread = (k = pt/4, quarter q = pt%4): 32 rows at one k, per-row scales;
-//     rows 8j..8j+7 at k at j*1024 + (k/8)*128 + (k%8)*16 (no swizzle; LBO 128 along k, SBO 1024 along m).
-template <int PH>
-__device__ __forceinline__ void decode_stage(uint32_t a_base, const uint8_t *slab, int kt, int pt, uint4 raw,
-                                             uint32_t fac) {
+// 32 lanes x 16 consecutive f32 columns of tensor memory -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded wait by lane 0 of a warp, result broadcast to the warp. On timeout: record it, raise the CTA's
+// abort flag and return false; once the flag is up every wait returns false at once, so each role leaves
+// (or, for the epilogue, runs out) its item loop without waiting again.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int lane, volatile int *abort_flag,
+                                          int *status) {
+    bool ok = true;
+    if (lane == 0) {
+        ok = !*abort_flag && mbar_wait(bar, parity);
+        if (!ok) {
+            set_error(status, DEV_ERR_TIMEOUT);
+            *abort_flag = 1;
+        }
+    }
+    return __shfl_sync(0xffffffffu, ok, 0);
+}
+
+__device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+    const bool ok = !*abort_flag && mbar_wait(bar, parity);
+    if (!ok) {
+        set_error(status, DEV_ERR_TIMEOUT);
+        *abort_flag = 1;
+    }
+    return ok;
+}
+
+// Decodes one 16-byte raw chunk (32 e2m1 codes) of a K-major row into four 8-code chunks of the A tile:
+// chunk c of row m at (m/8)*1024 + c*128 + (m%8)*16 (no swizzle; LBO 128 along k, SBO 1024 along m).
+// sc: the two e4m3 scales of the 32 codes as f16x2 (times the down factor).
+__device__ __forceinline__ void put_kmajor(uint32_t a_tile, int m, int c0, uint4 raw, __half2 sc) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    if (PH == PH_UP || PH == PH_DN_O) {
-        constexpr int GP = PH == PH_UP ? G_UP : G_DN;
-        const int m = pt >> 1, hf = pt & 1;
-        const uint16_t s01 = *reinterpret_cast<const uint16_t *>(slab + m * GP + kt * 4 + hf * 2);
-        __half2 sc = as_h2(e4m3x2_f16x2(s01));
-        if (PH == PH_DN_O) sc = __hmul2(sc, as_h2(fac));
-        const __half2 sa = __low2half2(sc), sb = __high2half2(sc);
-        const uint32_t row = a_base + (m >> 3) * 1024 + (m & 7) * 16;
+    const __half2 sa = __low2half2(sc), sb = __high2half2(sc);
+    const uint32_t row = a_tile + (m >> 3) * 1024 + (m & 7) * 16;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            uint32_t o[4];
-            e2m1x8_f16x2(w[i], o);
-            const __half2 s = i < 2 ? sa : sb;
-            st_shared_v4(row + (hf * 4 + i) * 128, h2_as_u(__hmul2(as_h2(o[0]), s)), h2_as_u(__hmul2(as_h2(o[1]), s)),
-                         h2_as_u(__hmul2(as_h2(o[2]), s)), h2_as_u(__hmul2(as_h2(o[3]), s)));
-        }
-    } else {
-        const int kl = pt >> 2, q = pt & 3;
-        const int g = (kt * BK + kl) >> 4;
-        const uint8_t *srow = slab + g * BM + q * 32;
-        const uint32_t kaddr = a_base + (kl >> 3) * 128 + (kl & 7) * 16;
-        const __half2 f = as_h2(fac);
+    for (int i = 0; i < 4; i++) {
+        uint32_t o[4];
+        e2m1x8_f16x2(w[i], o);
+        const __half2 s = i < 2 ? sa : sb;
+        st_shared_v4(row + (c0 + i) * 128, h2_as_u(__hmul2(as_h2(o[0]), s)), h2_as_u(__hmul2(as_h2(o[1]), s)),
+                     h2_as_u(__hmul2(as_h2(o[2]), s)), h2_as_u(__hmul2(as_h2(o[3]), s)));
+    }
+}
+
+// Decodes one 16-byte raw chunk of the T layout (32 output rows 32q..32q+31 at input neuron kl) into the
+// MN-major A tile: rows 8j..8j+7 at k = kl sit at j*1024 + (kl/8)*128 + (kl%8)*16 (LBO 128 along k,
+// SBO 1024 along m). srow: the 32 e4m3 scales of those rows; f: the down factor.
+__device__ __forceinline__ void put_mnmajor(uint32_t a_tile, int kl, int q, uint4 raw, const uint8_t *srow, __half2 f) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const uint32_t kaddr = a_tile + (kl >> 3) * 128 + (kl & 7) * 16;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint2 s8 = *reinterpret_cast<const uint2 *>(srow + i * 8);
-            uint32_t s[4];
-            e4m3x4_f16x2(s8.x, s[0], s[1]);
-            e4m3x4_f16x2(s8.y, s[2], s[3]);
-            uint32_t o[4];
-            e2m1x8_f16x2(w[i], o);
-            st_shared_v4(kaddr + (q * 4 + i) * 1024, h2_as_u(__hmul2(as_h2(o[0]), __hmul2(as_h2(s[0]), f))),
-                         h2_as_u(__hmul2(as_h2(o[1]), __hmul2(as_h2(s[1]), f))),
-                         h2_as_u(__hmul2(as_h2(o[2]), __hmul2(as_h2(s[2]), f))),
-                         h2_as_u(__hmul2(as_h2(o[3]), __hmul2(as_h2(s[3]), f))));
-        }
+    for (int i = 0; i < 4; i++) {
+        const uint2 s8 = *reinterpret_cast<const uint2 *>(srow + i * 8);
+        uint32_t s[4];
+        e4m3x4_f16x2(s8.x, s[0], s[1]);
+        e4m3x4_f16x2(s8.y, s[2], s[3]);
+        uint32_t o[4];
+        e2m1x8_f16x2(w[i], o);
+        st_shared_v4(kaddr + (q * 4 + i) * 1024, h2_as_u(__hmul2(as_h2(o[0]), __hmul2(as_h2(s[0]), f))),
+                     h2_as_u(__hmul2(as_h2(o[1]), __hmul2(as_h2(s[1]), f))),
+                     h2_as_u(__hmul2(as_h2(o[2]), __hmul2(as_h2(s[2]), f))),
+                     h2_as_u(__hmul2(as_h2(o[3]), __hmul2(as_h2(s[3]), f))));
     }
 }
 
 // Smallest h-block scale exponent of a tile (the block with the largest amax) over its 21 up blocks,
-// reduced across one warp; lane l < 21 also returns its own block's exponent in *mine.
-__device__ __forceinline__ int tile_s0(const Params &p, int tile, int lane, int *mine) {
-    const int s = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
-    int m = s;
+// reduced across one warp.
+__device__ __forceinline__ int tile_s0(const Params &p, int tile, int lane) {
+    int m = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
-    *mine = s;
     return m;
 }
 
-// The grouped GEMM. grid = (row blocks, tile capacity); CTAs past the tile count exit at once.
+// The grouped GEMM, persistent: one CTA per SM walks the items (tile, 128-row block) i = blockIdx.x,
+// blockIdx.x + gridDim.x, ...; consecutive items share a tile (its activations stay in L2).
+// Roles: warp 12 streams each item's scales (one copy) and its raw weights (16 KB TMA boxes of 256 k) into
+// a 3-deep ring; warps 4..11 decode them into f16 A stages (64 k each); warp 13 loads the activation (B)
+// stages with TMA (one box of 16..128 pair rows per k-stage); warp 14 issues tcgen05.mma into one of two
+// TMEM accumulators while warps 0..3 drain the other one (epilogue).
 template <int PH>
-__global__ void __launch_bounds__(THREADS, 1) pf_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tmb) {
+__global__ void __launch_bounds__(THREADS, 1)
+    pf_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_b16, const __grid_constant__ CUtensorMap tm_b32,
+                   const __grid_constant__ CUtensorMap tm_b64, const __grid_constant__ CUtensorMap tm_b128,
+                   const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
+                   const __grid_constant__ CUtensorMap tm_s) {
+    constexpr int MT = PH == PH_UP ? MT_UP : MT_DN;
     constexpr int NKT = PH == PH_UP ? NKT_UP : NKT_DN;
-    const int mt = blockIdx.x;
-    const int tile = blockIdx.y;
-    if (tile >= *p.tile_count) return;
-    const int4 td = p.tiles[tile];
-    const int e = td.x, n0 = td.y, n = td.z;
-    const int N = (n + 15) & ~15;
-    const uint8_t *blk = p.store + (int64_t)e * p.bstride;
+    constexpr int NKR = (NKT + KPR - 1) / KPR;
+    const int nitems = *p.tile_count * MT;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     uint8_t *sm = smem_raw + (((raw_base + 1023u) & ~1023u) - raw_base);
     const uint32_t sbase = smem_u32(sm);
-    uint8_t *slab = sm + OFF_SLAB;
     float *colsc = reinterpret_cast<float *>(sm + OFF_COLSC);
-    uint32_t *sfac = reinterpret_cast<uint32_t *>(sm + OFF_SFAC);
     float *red = reinterpret_cast<float *>(sm + OFF_RED);
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
-    uint64_t *empty = full + STAGES;
-    uint64_t *accb = empty + STAGES;
+    __half *stg = reinterpret_cast<__half *>(sm + OFF_STG);
+    uint64_t *a_full = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
+    uint64_t *a_empty = a_full + SA;
+    uint64_t *b_full = a_empty + SA;
+    uint64_t *b_empty = b_full + SB;
+    uint64_t *raw_full = b_empty + SB;
+    uint64_t *raw_empty = raw_full + SR;
+    uint64_t *acc_full = raw_empty + SR;
+    uint64_t *acc_empty = acc_full + 2;
+    uint64_t *slab_full = acc_empty + 2;
+    uint64_t *slab_empty = slab_full + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF_ABORT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], NPROD + 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < SA; s++) {
+            mbar_init(&a_full[s], NDEC / 32);
+            mbar_init(&a_empty[s], 1);
         }
-        mbar_init(accb, 1);
+        for (int s = 0; s < SB; s++) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&b_empty[s], 1);
+        }
+        for (int r = 0; r < SR; r++) {
+            mbar_init(&raw_full[r], 1);
+            mbar_init(&raw_empty[r], NDEC / 32);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 4);
+            mbar_init(&slab_full[a], 1);
+            mbar_init(&slab_empty[a], NDEC / 32);
+        }
+        *abort_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 0) {
+    if (warp == W_MMA) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TMEM_COLS)
                      : "memory");
@@ -459,160 +529,276 @@ __global__ void __launch_bounds__(THREADS, 1) pf_gemm_kernel(const Params p, con
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp >= 4) {
-        // ------------------------------------------------------------------ producers
-        const int pt = tid - 128;
-        if (PH == PH_UP) {
-            const uint8_t *src = blk + O_US + (int64_t)mt * BM * G_UP;
-            for (int i = pt; i < BM * G_UP / 16; i += NPROD)
-                reinterpret_cast<uint4 *>(slab)[i] = ldg_stream(src + i * 16);
-        } else if (PH == PH_DN_O) {
-            const uint8_t *src = blk + O_DS + (int64_t)mt * BM * G_DN;
-            for (int i = pt; i < BM * G_DN / 16; i += NPROD)
-                reinterpret_cast<uint4 *>(slab)[i] = ldg_stream(src + i * 16);
-        } else {
-            for (int i = pt; i < G_DN * (BM / 16); i += NPROD) {
-                const int g = i >> 3, q = i & 7;
-                reinterpret_cast<uint4 *>(slab + g * BM)[q] = ldg_stream(blk + O_DS + (int64_t)g * LAT + mt * BM + q * 16);
+    if (warp == W_RAW) {
+        // ------------------------------------------------------------ scales (per item) + raw weights -> rings
+        if (lane == 0) {
+            uint32_t q = 0;
+            int e_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].x : 0;   // one item ahead
+            for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
+                const int mt = i % MT;
+                const int e = e_next;
+                if (i + (int)gridDim.x < nitems) e_next = p.tiles[(i + gridDim.x) / MT].x;
+                const uint8_t *blk = p.store + (int64_t)e * p.bstride;
+                const int sb = j & 1;
+                if (!lane_wait(&slab_empty[sb], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+                uint8_t *slab = sm + OFF_SLAB + sb * SLAB_BYTES;
+                if (PH == PH_UP) {
+                    mbar_expect_tx(&slab_full[sb], BM * G_UP);
+                    bulk_g2s(slab, blk + O_US + (int64_t)mt * BM * G_UP, BM * G_UP, &slab_full[sb], policy_evict_first());
+                } else if (PH == PH_DN_O) {
+                    mbar_expect_tx(&slab_full[sb], BM * G_DN);
+                    bulk_g2s(slab, blk + O_DS + (int64_t)mt * BM * G_DN, BM * G_DN, &slab_full[sb], policy_evict_first());
+                } else {
+                    mbar_expect_tx(&slab_full[sb], BM * G_DN);
+                    tma_load_3d(slab, &tm_s, mt * BM, ROW1024_DNT_S, e, &slab_full[sb]);
+                }
+                bool ok = true;
+                for (int kr = 0; kr < NKR; kr++, q++) {
+                    const int r = q % SR;
+                    if (!lane_wait(&raw_empty[r], ((q / SR) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *dst = sm + OFF_RAW + r * RAW_BYTES;
+                    if (PH == PH_UP) {
+                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
+                        tma_load_3d(dst, &tm_w, kr * (RK / 2), mt * BM, e, &raw_full[r]);
+                    } else if (PH == PH_DN_T) {
+                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
+                        tma_load_3d(dst, &tm_w, mt * (BM / 2), ROW512_DNT + kr * RK, e, &raw_full[r]);
+                    } else {
+                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
+                        tma_load_3d(dst, &tm_w, kr * (RK / 2), ROW1344_DW + mt * BM, e, &raw_full[r]);
+                    }
+                }
+                if (!ok) break;
             }
         }
-        if (PH != PH_UP && warp == 4) {
-            int mine;
-            const int s0 = tile_s0(p, tile, lane, &mine);
-            if (lane < MT_UP) sfac[lane] = pow2_h2(s0 - mine);
-        }
-        named_sync(1, NPROD);
-
-        uint4 pre[PF];
-#pragma unroll
-        for (int i = 0; i < PF; i++) pre[i] = load_raw<PH>(blk, mt, i, pt);
-        bool ok = true;
-        for (int kt0 = 0; kt0 < NKT && ok; kt0 += PF) {
-#pragma unroll
-            for (int i = 0; i < PF; i++) {
-                const int kt = kt0 + i;
-                if (kt >= NKT) break;
-                const uint4 cur = pre[i];
-                if (kt + PF < NKT) pre[i] = load_raw<PH>(blk, mt, kt + PF, pt);
-                const int s = kt % STAGES;
-                const uint32_t use = kt / STAGES;
-                if (!mbar_wait(&empty[s], (use & 1u) ^ 1u)) {
-                    set_error(p.status, DEV_ERR_TIMEOUT);
-                    ok = false;
-                    break;
+        __syncwarp();
+    } else if (warp == W_B) {
+        // ------------------------------------------------------------ activations (B) -> ring
+        if (lane == 0) {
+            uint32_t c = 0;
+            int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
+            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
+                const int4 td = td_next;
+                if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
+                const int n0 = td.y, N = (td.z + 15) & ~15;
+                const CUtensorMap *map = N <= 16 ? &tm_b16 : N <= 32 ? &tm_b32 : N <= 64 ? &tm_b64 : &tm_b128;
+                const uint32_t bytes = (N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128) * 128;
+                bool ok = true;
+                for (int kt = 0; kt < NKT; kt++, c++) {
+                    const int s = c % SB;
+                    if (!lane_wait(&b_empty[s], ((c / SB) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&b_full[s], bytes);
+                    tma_load_2d(sm + OFF_B + s * B_BYTES, map, kt * BK, n0, &b_full[s]);
                 }
-                uint8_t *a_tile = sm + s * STAGE_BYTES;
-                if (pt == 0) {
-                    mbar_expect_tx(&full[s], (uint32_t)(N / 16) * BOX_BYTES);
-                    for (int b = 0; b < N / 16; b++)
-                        tma_load_2d(a_tile + A_BYTES + b * BOX_BYTES, &tmb, kt * BK, n0 + b * 16, &full[s]);
-                }
-                decode_stage<PH>(sbase + s * STAGE_BYTES, slab, kt, pt, cur, PH == PH_UP ? 0u : sfac[kt >> 1]);
-                fence_async_smem();
-                mbar_arrive(&full[s]);
+                if (!ok) break;
             }
         }
-    } else {
-        // ------------------------------------------------------------------ MMA issue (warp 0) + epilogue
-        if (warp == 0) {
-            const uint32_t idesc = instr_desc_f16(N, PH == PH_DN_T);
-            bool ok = true;
-            for (int kt = 0; kt < NKT; kt++) {
-                const int s = kt % STAGES;
-                const uint32_t use = kt / STAGES;
-                if (lane == 0) ok = mbar_wait(&full[s], use & 1u);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
-                    if (lane == 0) set_error(p.status, DEV_ERR_TIMEOUT);
-                    break;
-                }
+        __syncwarp();
+    } else if (warp == W_MMA) {
+        // ------------------------------------------------------------ tcgen05.mma issue
+        if (lane == 0) {
+            uint32_t c = 0;
+            int n_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].z : 0;
+            for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
+                const int n = n_next;
+                if (i + (int)gridDim.x < nitems) n_next = p.tiles[(i + gridDim.x) / MT].z;
+                const int a = j & 1;
+                if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a0 = sbase + s * STAGE_BYTES;
-                    const uint32_t b0 = a0 + A_BYTES;
+                const uint32_t idesc = instr_desc_f16((n + 15) & ~15, PH == PH_DN_T);
+                const uint32_t d = tmem + a * NT;
+                bool ok = true;
+                for (int kt = 0; kt < NKT; kt++, c++) {
+                    const int sa = c % SA, sb = c % SB;
+                    if (!lane_wait(&a_full[sa], (c / SA) & 1, abort_flag, p.status) ||
+                        !lane_wait(&b_full[sb], (c / SB) & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a0 = sbase + OFF_A + sa * A_BYTES;
+                    const uint32_t b0 = sbase + OFF_B + sb * B_BYTES;
 #pragma unroll
                     for (int k = 0; k < BK / 16; k++) {
                         const uint64_t ad = smem_desc(a0 + k * 256, 128, 1024, 0);
                         const uint64_t bd = smem_desc(b0 + k * 32, 16, 1024, 2);
-                        mma_f16(tmem, ad, bd, idesc, (kt | k) != 0);
+                        mma_f16(d, ad, bd, idesc, (kt | k) != 0);
                     }
-                    mma_commit(&empty[s]);
+                    mma_commit(&a_empty[sa]);
+                    mma_commit(&b_empty[sb]);
                 }
+                mma_commit(&acc_full[a]);   // also after a failed wait: tracks every MMA issued
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ decoders: raw ring -> f16 A stages
+        const int dt = tid - 128;
+        uint32_t q = 0, c = 0;
+        // h-block exponents of the tile, one item ahead (down only)
+        int s_next = (PH != PH_UP && blockIdx.x < nitems && lane < MT_UP)
+                         ? p.tile_scale[(int64_t)(blockIdx.x / MT) * MT_UP + lane] : INT_MAX;
+        for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
+            uint32_t myfac = 0x3C003C00u;   // 1.0 in f16x2
+            if (PH != PH_UP) {
+                const int mine = s_next;
+                if (i + (int)gridDim.x < nitems && lane < MT_UP)
+                    s_next = p.tile_scale[(int64_t)((i + gridDim.x) / MT) * MT_UP + lane];
+                int s0 = mine;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
+                myfac = lane < MT_UP ? pow2_h2(s0 - mine) : 0u;
+            }
+            const int sbf = j & 1;
+            if (!warp_wait(&slab_full[sbf], (j >> 1) & 1, lane, abort_flag, p.status)) break;
+            const uint8_t *slab = sm + OFF_SLAB + sbf * SLAB_BYTES;
+            bool ok = true;
+            for (int kr = 0; kr < NKR; kr++, q++) {
+                const int r = q % SR;
+                const int kc = min(KPR, NKT - kr * KPR);   // A stages filled from this raw stage
+                bool got = warp_wait(&raw_full[r], (q / SR) & 1, lane, abort_flag, p.status);
+                for (int t = 0; t < kc && got; t++)
+                    got = warp_wait(&a_empty[(c + t) % SA], (((c + t) / SA) & 1) ^ 1, lane, abort_flag, p.status);
+                if (!got) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t *rw = sm + OFF_RAW + r * RAW_BYTES;
+#pragma unroll
+                for (int u = 0; u < UNITS; u++) {
+                    const int unit = dt + NDEC * u;
+                    if (PH == PH_DN_T) {
+                        const int n = unit >> 2, q4 = unit & 3;   // input neuron within the stage, 32-row group
+                        const int t = n >> 6;
+                        // h block of this k-stage (128 neurons each): its factor 2^(S0 - S_block)
+                        const uint32_t f = __shfl_sync(0xffffffffu, myfac, ((kr * KPR + t) >> 1) & 31);
+                        if (t < kc) {
+                            const uint4 raw = *reinterpret_cast<const uint4 *>(rw + n * (BM / 2) + q4 * 16);
+                            const int g = (kr * RK + n) >> 4;
+                            put_mnmajor(sbase + OFF_A + ((c + t) % SA) * A_BYTES, n & 63, q4, raw,
+                                        slab + g * BM + q4 * 32, as_h2(f));
+                        }
+                    } else {
+                        const int row = unit / PPR, part = unit % PPR;   // weight row, 32-code part of the stage
+                        const int t = part >> 1;
+                        const uint32_t f = __shfl_sync(0xffffffffu, myfac, ((kr * KPR + t) >> 1) & 31);
+                        if (t < kc) {
+                            const uint4 raw = *reinterpret_cast<const uint4 *>(rw + row * (RK / 2) + part * 16);
+                            constexpr int GP = PH == PH_UP ? G_UP : G_DN;
+                            const uint16_t s01 =
+                                *reinterpret_cast<const uint16_t *>(slab + row * GP + kr * (RK / 16) + part * 2);
+                            __half2 sc = as_h2(e4m3x2_f16x2(s01));
+                            if (PH == PH_DN_O) sc = __hmul2(sc, as_h2(f));
+                            put_kmajor(sbase + OFF_A + ((c + t) % SA) * A_BYTES, row, (part & 1) * 4, raw, sc);
+                        }
+                    }
+                }
+                fence_async_smem();   // this thread's A writes -> visible to the tensor core (async proxy)
                 __syncwarp();
+                if (lane == 0) {
+                    for (int t = 0; t < kc; t++) mbar_arrive(&a_full[(c + t) % SA]);
+                    mbar_arrive(&raw_empty[r]);
+                }
+                c += kc;
             }
-            if (lane == 0) mma_commit(accb);   // also after a failed wait: tracks every MMA issued
+            if (!ok) break;
             __syncwarp();
+            if (lane == 0) mbar_arrive(&slab_empty[sbf]);
         }
-        // per-column factors
-        int s0 = 0;
-        if (PH != PH_UP) {
-            int mine;
-            s0 = tile_s0(p, tile, lane, &mine);
-        }
-        for (int j = tid; j < n; j += 128) {
-            if (PH == PH_UP) colsc[j] = pow2f(-p.pair_exp[n0 + j]) * p.s2[(int64_t)e * 2];
-            else colsc[j] = p.pair_coef[n0 + j] * p.s2[(int64_t)e * 2 + 1] * pow2f(-s0);
-        }
-        named_sync(2, 128);
-        const bool acc_ok = mbar_wait(accb, 0);
-        if (!acc_ok && tid == 0) set_error(p.status, DEV_ERR_TIMEOUT);
-        tc_fence_after();
-        const int m = tid;   // accumulator row = TMEM lane
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
-        if (PH == PH_UP) {
-            // pass 1: amax of h over the 128 x n block (every thread reaches the same barriers)
-            float mx = 0.f;
-            if (acc_ok) {
-                for (int c0 = 0; c0 < n; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(trow + c0, v);
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 0..3 = TMEM lanes)
+        const int m = tid;
+        // no early exit: the four warps must take the same named barriers for every item
+        for (int i = blockIdx.x, j = 0; i < nitems; i += gridDim.x, j++) {
+            const int tile = i / MT, mt = i % MT;
+            const int4 td = p.tiles[tile];
+            const int e = td.x, n0 = td.y, n = td.z;
+            const int a = j & 1;
+            float *cs = colsc + a * NT;
+            const int s0 = PH != PH_UP ? tile_s0(p, tile, lane) : 0;
+            for (int jj = tid; jj < n; jj += 128) {
+                if (PH == PH_UP) cs[jj] = pow2f(-p.pair_exp[n0 + jj]) * p.s2[(int64_t)e * 2];
+                else cs[jj] = p.pair_coef[n0 + jj] * p.s2[(int64_t)e * 2 + 1] * pow2f(-s0);
+            }
+            named_sync(1, 128);
+            const bool acc_ok = warp_wait(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
+            tc_fence_after();
+            const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
+            if (PH == PH_UP) {
+                // pass 1: amax of h over the 128 x n block (every thread reaches the same barriers)
+                float mx = 0.f;
+                if (acc_ok) {
+                    for (int c0 = 0; c0 < n; c0 += 32) {
+                        float v[32];
+                        tmem_ld32(trow + c0, v);
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (c0 + j < n) {
-                            const float u = v[j] * colsc[c0 + j];
-                            mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
+                        for (int jj = 0; jj < 32; jj++) {
+                            if (c0 + jj < n) {
+                                const float u = v[jj] * cs[c0 + jj];
+                                mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
+                            }
                         }
                     }
                 }
-            }
 #pragma unroll
-            for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            if (lane == 0) red[warp] = mx;
-            named_sync(2, 128);
-            mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-            // an all-zero block takes the largest exponent so that it never sets the tile's reference
-            const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
-            if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
-            // pass 2: h * 2^S as f16 (the block's amax lands in [2^14, 2^15))
-            if (acc_ok) {
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (lane == 0) red[a * 4 + warp] = mx;
+                named_sync(1, 128);
+                mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
+                // an all-zero block takes the largest exponent so that it never sets the tile's reference
+                const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
+                if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
+                // pass 2: h * 2^S as f16 (the block's amax lands in [2^14, 2^15)), staged through shared
+                // memory 16 pairs at a time so that each pair's 128 values go out as 16-byte stores
                 const float sc = pow2f(S);
-                __half *dst = p.hs + (int64_t)n0 * INTER + mt * BM + m;
+                for (int c0 = 0; c0 < n; c0 += STG_COLS) {
+                    if (acc_ok) {
+                        float v[16];
+                        tmem_ld16(trow + c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < STG_COLS; jj++) {
+                            const float u = v[jj] * cs[(c0 + jj) & (NT - 1)];
+                            stg[jj * BM + m] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
+                        }
+                    }
+                    named_sync(1, 128);
+                    if (acc_ok) {
+#pragma unroll
+                        for (int k2 = 0; k2 < 2; k2++) {
+                            const int piece = tid + 128 * k2;
+                            const int row = piece >> 4, part = piece & 15;
+                            if (c0 + row < n)
+                                *reinterpret_cast<uint4 *>(p.hs + (int64_t)(n0 + c0 + row) * INTER + mt * BM + part * 8) =
+                                    *reinterpret_cast<const uint4 *>(stg + row * BM + part * 8);
+                        }
+                    }
+                    named_sync(1, 128);
+                }
+            } else if (acc_ok) {
+                float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
                 for (int c0 = 0; c0 < n; c0 += 32) {
                     float v[32];
                     tmem_ld32(trow + c0, v);
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        if (c0 + j < n) {
-                            const float u = v[j] * colsc[c0 + j];
-                            dst[(int64_t)(c0 + j) * INTER] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
-                        }
-                    }
+                    for (int jj = 0; jj < 32; jj++)
+                        if (c0 + jj < n) dst[(int64_t)(c0 + jj) * LAT] = v[jj] * cs[c0 + jj];
                 }
             }
-        } else if (acc_ok) {
-            float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
-            for (int c0 = 0; c0 < n; c0 += 32) {
-                float v[32];
-                tmem_ld32(trow + c0, v);
-#pragma unroll
-                for (int j = 0; j < 32; j++)
-                    if (c0 + j < n) dst[(int64_t)(c0 + j) * LAT] = v[j] * colsc[c0 + j];
-            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == W_MMA) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }
@@ -673,16 +859,31 @@ inline EncodeTiledFn encode_tiled() {
     return fn;
 }
 
-// Row-major f16 matrix [rows, cols] -> map with 64 x 16 boxes and 128-byte swizzle.
-inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols) {
+// Row-major f16 matrix [rows, cols] -> map with {64, box_rows} boxes and 128-byte swizzle.
+inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int box_rows) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {BK, BOX_ROWS};
+    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The store as a u8 tensor [ne][BLOCK / pitch][pitch] (expert stride bstride), for TMA boxes of
+// {box_x bytes, box_y rows} out of one block region.
+inline bool make_store_map(CUtensorMap *m, const void *store, int64_t bstride, int ne, int pitch, int box_x,
+                           int box_y) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)(BLOCK / pitch), (cuuint64_t)ne};
+    const cuuint64_t strides[2] = {(cuuint64_t)pitch, (cuuint64_t)bstride};
+    const cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)box_y, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(store), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -717,7 +918,6 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     int dev;
     DeviceInfo *di;
     if (int rc = current_device(&dev, &di)) return rc;
-    (void)di;
 
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     Params p{};
@@ -750,9 +950,15 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.hs = reinterpret_cast<__half *>(ws + L.hs);
     p.op = reinterpret_cast<float *>(ws + L.op);
 
-    CUtensorMap map_x, map_h;
-    if (!make_map(&map_x, p.xp, L.P, LAT) || !make_map(&map_h, p.hs, L.P, INTER)) return QMOE_ERR_LAUNCH;
-
+    CUtensorMap bx[4], bh[4], wu, wd, sd;
+    const int hts[4] = {16, 32, 64, 128};
+    for (int k = 0; k < 4; k++)
+        if (!make_map(&bx[k], p.xp, L.P, LAT, hts[k]) || !make_map(&bh[k], p.hs, L.P, INTER, hts[k])) return QMOE_ERR_LAUNCH;
+    if (!make_store_map(&wu, store, block_stride, n_experts, 512, RK / 2, BM) ||
+        !make_store_map(&wd, store, block_stride, n_experts, layout_T ? 512 : 1344, layout_T ? BM / 2 : RK / 2,
+                        layout_T ? RK : BM) ||
+        !make_store_map(&sd, store, block_stride, n_experts, 1024, BM, G_DN))
+        return QMOE_ERR_LAUNCH;
     auto up = pf_gemm_kernel<PH_UP>;
     auto dn = layout_T ? pf_gemm_kernel<PH_DN_T> : pf_gemm_kernel<PH_DN_O>;
     if (!ensure_smem(up, SMEM_BYTES, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
@@ -763,8 +969,8 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
     pf_gather_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-    up<<<dim3(MT_UP, L.tiles_cap), THREADS, SMEM_BYTES, st>>>(p, map_x);
-    dn<<<dim3(MT_DN, L.tiles_cap), THREADS, SMEM_BYTES, st>>>(p, map_h);
+    up<<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bx[0], bx[1], bx[2], bx[3], wu, wu, wu);
+    dn<<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wd, wd, sd);
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
 }
