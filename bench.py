@@ -47,7 +47,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "dense"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "dense", "prefill", "ep"])
+    ap.add_argument("--ep-t", type=int, default=64, help="ep workload: tokens per rank per step (config 4 decode batch)")
+    ap.add_argument("--prefill-t", type=int, default=2048, help="prefill workload: tokens per call (config 3)")
     return ap.parse_args()
 
 
@@ -335,10 +337,227 @@ def run_dense(args):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_FLOP_PER_PAIR = 2 * (2688 * 1024 + 1024 * 2688)   # up + down MACs x 2 = 11,010,048
+
+
+def run_prefill(args):
+    """the prompt path, one MoE layer of 512 synthetic NVFP4 experts (T layout, 1.585 GB
+    resident in HBM), T tokens drawn as in config 0 and routed top-22 by the synthetic router; one step =
+    one qmoe_prefill_grouped call (routing sort, activation gather, up GEMM + ReLU^2, down GEMM, combine).
+    value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call with the
+    token block and routing copied from pinned host memory and the output copied back, every step."""
+    import torch
+    import qmoe_ns as Q
+    import qmoe_synth as S
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    hbm, peak_kind = peaks()
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tpk = json.load(f)
+        tflops = float(tpk.get("bf16_tflops_sustained", tpk.get("bf16_tflops")))
+        tkind = "measured (cuBLAS bf16, sustained)"
+    except Exception:
+        tflops, tkind = 1400.0, "fallback"
+    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303)
+    s2l = s2[0].contiguous()
+    g = S.seeded(404, dev)
+    T = args.prefill_t
+    X = S.tokens(T, m_hats[0], g, dev)
+    ids, w = S.route(X, *routers[0])
+    ids = ids.to(torch.int32).contiguous()
+    w = w.float().contiguous()
+    uniq = int(torch.unique(ids).numel())
+    out = torch.empty(T, S.LAT, device=dev)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for _ in range(max(3, args.warmup)):
+            Q.moe_prefill(store, ids, w, s2l, X, out=out)
+        st.synchronize()
+        if Q.prefill_status() != 0:
+            raise RuntimeError("prefill kernels reported a device-side error")
+        clk = Clocks(0)
+        clk.start()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            Q.moe_prefill(store, ids, w, s2l, X, out=out)
+        e1.record(st)
+        e1.synchronize()
+        clocks = clk.stop()
+        ms = e0.elapsed_time(e1) / args.steps
+        # e2e: host inputs (pinned) -> device, call, output -> host, every step
+        hx = X.cpu().pin_memory()
+        hid = ids.cpu().pin_memory()
+        hw = w.cpu().pin_memory()
+        hout = torch.empty(T, S.LAT, dtype=torch.float32).pin_memory()
+        dx, did, dw = torch.empty_like(X), torch.empty_like(ids), torch.empty_like(w)
+        ee = max(5, args.steps // 2)
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record(st)
+        for _ in range(ee):
+            dx.copy_(hx, non_blocking=True)
+            did.copy_(hid, non_blocking=True)
+            dw.copy_(hw, non_blocking=True)
+            Q.moe_prefill(store, did, dw, s2l, dx, out=out)
+            hout.copy_(out, non_blocking=True)
+        e3.record(st)
+        e3.synchronize()
+        ms_e2e = e2.elapsed_time(e3) / ee
+    flop = T * K * PREFILL_FLOP_PER_PAIR
+    wbytes = uniq * S.BLOCK
+    act_bytes = T * S.LAT * 2 + T * S.LAT * 4 + T * K * 8
+    t_hbm = (wbytes + act_bytes) / (hbm * 1e6)      # ms
+    t_tc = flop / (tflops * 1e9)                    # ms
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+    if bound == "hbm":
+        roof = {"bound": "hbm", "achieved": round((wbytes + act_bytes) / ms / 1e6, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(t_hbm / ms, 4), "peak_kind": f"{peak_kind} (HBM copy)"}
+    else:
+        roof = {"bound": "tensor", "achieved": round(flop / ms / 1e9, 1), "peak": tflops, "unit": "TFLOP/s",
+                "frac": round(t_tc / ms, 4), "peak_kind": tkind}
+    roof["traffic"] = None
+    roof["algorithmic"] = {"flop": flop, "weight_bytes": wbytes, "activation_bytes": act_bytes,
+                           "t_hbm_ms": round(t_hbm, 4), "t_tensor_ms": round(t_tc, 4)}
+    line = {"metric": "MoE prefill tokens/s (one routed-expert layer, top-22 of 512)", "value": round(T / ms * 1e3, 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "nvfp4 x f16 -> f32 (tcgen05 kind::f16)", "data": "synthetic",
+            "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
+                       "unique_experts": uniq, "l2": "weights (1.585 GB) exceed L2"},
+            "roofline": roof, "clocks": clocks,
+            "e2e": {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
+                    "d2h_bytes_per_step": int(out.numel() * 4)},
+            "gpu_launches": 7 * args.steps}
+    print(json.dumps(line), flush=True)
+
+
+def run_ep(args):
+    """expert parallelism. The 512 experts of every layer are sharded over the N ranks
+    (expert e on rank e // (512 / N), T layout, resident in HBM); each rank holds a batch of --ep-t tokens.
+    A step = `--layers` MoE layers, each an ExpertParallelMoE forward: dispatch pack, NCCL all_to_all of the
+    token blocks and routing, the local experts (grouped tcgen05 GEMM), all_to_all of the partial outputs,
+    rank-order combine. value = tokens of all ranks per second of max-over-ranks device time."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    import ep as EP
+    import qmoe_ns as Q
+    import qmoe_synth as S
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world == 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29533")
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    L, T = args.layers, args.ep_t
+    el = NE // world
+    g = S.seeded(1234, dev)
+    # this rank's experts of every layer (generated on the device, converted to the T layout)
+    store = torch.empty(L * el, S.BLOCK, dtype=torch.uint8, device=dev)
+    s2 = torch.empty(L, el, 2, dtype=torch.float32, device=dev)
+    gl = S.seeded(99, dev)   # same m_hat / router on every rank
+    m_hats = [S.unit_dir(gl, dev) for _ in range(L)]
+    routers = [S.router(gl, dev) for _ in range(L)]
+    p_l = S.layer_live_fractions(L) if L > 1 else [0.075]
+    B = 16
+    for m in range(L):
+        for e0 in range(0, el, B):
+            nb = min(B, el - e0)
+            blk, s2b, _ = S.expert_blocks(nb, p_l[m], m_hats[m], g, dev)
+            store[m * el + e0:m * el + e0 + nb].copy_(blk)
+            s2[m, e0:e0 + nb] = s2b
+            del blk
+        Q.to_T_batch(store[m * el:(m + 1) * el])
+    layers = [EP.ExpertParallelMoE(store[m * el:(m + 1) * el], s2[m], n_experts=NE) for m in range(L)]
+    gx = S.seeded(555 + rank, dev)
+    X = [S.tokens(T, m_hats[m], gx, dev) for m in range(L)]
+    R = [S.route(X[m], *routers[m]) for m in range(L)]
+
+    def step():
+        outs = []
+        for m in range(L):
+            outs.append(layers[m](X[m], R[m][0], R[m][1]))
+        return outs
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if Q.prefill_status() != 0:
+        raise RuntimeError("expert kernels reported a device-side error")
+    clk = Clocks(local)
+    if rank == 0:
+        clk.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clocks = clk.stop() if rank == 0 else None
+    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    # e2e through the public module: host token blocks + routing in, host outputs back, every step
+    hX = [x.cpu().pin_memory() for x in X]
+    hI = [r[0].cpu().pin_memory() for r in R]
+    hW = [r[1].cpu().pin_memory() for r in R]
+    hO = torch.empty(L, T, S.LAT, dtype=torch.float32).pin_memory()
+    ee = max(3, args.steps // 2)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record()
+    for _ in range(ee):
+        for m in range(L):
+            y = layers[m](hX[m].to(dev, non_blocking=True), hI[m].to(dev, non_blocking=True), hW[m].to(dev, non_blocking=True))
+            hO[m].copy_(y, non_blocking=True)
+    e3.record()
+    e3.synchronize()
+    me = torch.tensor([e2.elapsed_time(e3) / ee], device=dev)
+    dist.all_reduce(me, op=dist.ReduceOp.MAX)
+    me = float(me.item())
+    if rank == 0:
+        toks = T * world
+        line = {"metric": "MoE expert-parallel tokens/s (40-layer routed experts, top-22 of 512)",
+                "value": round(toks / ms * 1e3, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 x f16 -> f32 (tcgen05 kind::f16)",
+                "data": "synthetic",
+                "config": {"workload": f"config4: EP{world}, {T} tokens per rank, {L} layers", "layers": L,
+                           "tokens_per_rank": T, "experts_per_rank": el, "parallelism": f"ep{world}",
+                           "exchange": "NCCL all_to_all, fixed T-row blocks"},
+                "clocks": clocks,
+                "e2e": {"value": round(toks / me * 1e3, 1), "unit": "tokens/s",
+                        "h2d_bytes_per_step": int(L * T * (S.LAT * 2 + K * 12)),
+                        "d2h_bytes_per_step": int(L * T * S.LAT * 4)},
+                "gpu_launches": L * args.steps * (2 + 7 + 1)}
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
+    if args.workload == "ep":
+        return run_ep(args)
     if args.workload == "dense":
         return run_dense(args)
     import torch

@@ -137,7 +137,8 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
  * accumulation; h is kept as f16 with power-of-two block scales). Expert e's block is at
  * store + e * block_stride (block_stride >= BLOCK, multiple of 16); layout_T selects the T layout of the
  * down half (else the orig layout). s2 [n_experts, 2] f32; x [T,1024] in x_dtype (bf16 is converted
- * exactly); out [T,1024] f32. An id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
+ * exactly); out [T,1024] f32. Id -1 means "no expert" (the pair is skipped; expert-parallel blocks use it for
+ * experts on other ranks); any other id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
  * and makes that token's output NaN. 1 <= T <= 65536, 1 <= topk <= 32, 1 <= n_experts <= 1024.
  * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts) bytes, 256-byte aligned) holds the
  * sorted pairs and the f16 activations of every pair; its status word must start at zero. */
@@ -145,6 +146,23 @@ size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts);
 int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
                          const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
                          void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------ expert parallelism */
+
+/* No counterpart in the reference (it runs every expert on one GPU). Expert e lives on rank
+ * e / (n_experts / world). Dispatch pack of one rank's T tokens for a fixed-size all-to-all: for every
+ * destination rank d, the tokens with at least one expert on d, in token order, fill rows 0..send_cnt[d)-1 of
+ * block d. send_x [world, T, 1024] (x's dtype); send_meta [world, T, 2*topk] i32: the block-local expert ids
+ * (-1 for experts on other ranks and for unused rows) then the routing weights as f32 bits; row_of [world, T]
+ * i32: row of token t in block d or -1; send_cnt [world] i32. */
+int qmoe_ep_dispatch_pack(const void *x, int x_dtype, const int32_t *ids, const float *weights, int T, int topk,
+                          int n_experts, int world, void *send_x, int32_t *send_meta, int32_t *row_of,
+                          int32_t *send_cnt, void *stream);
+
+/* No counterpart in the reference. Combine after the return all-to-all: recv_part [world, T, 1024] f32 holds,
+ * in block d, rank d's partial outputs for the rows this rank packed for d; out[t] = sum over d in rank
+ * order of recv_part[d, row_of[d, t]] (rows with row_of -1 skipped). */
+int qmoe_ep_combine(const float *recv_part, const int32_t *row_of, int T, int world, float *out, void *stream);
 
 /* ------------------------------------------------------------------ layouts */
 

@@ -36,6 +36,8 @@ SIGNATURES = {
     "qmoe_pairs": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qmoe_prefill_workspace_bytes": (_sz, [_i, _i, _i]),
     "qmoe_prefill_grouped": (_i, [_p, _i64, _i, _i, _p, _p, _p, _p, _i, _i, _i, _p, _p, _sz, _p]),
+    "qmoe_ep_dispatch_pack": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p]),
+    "qmoe_ep_combine": (_i, [_p, _p, _i, _i, _p, _p]),
     "qmoe_from_T": (_i, [_p, _i, _p, _p]),
     "qmoe_to_T": (_i, [_p, _i, _p, _p]),
     "qmoe_deq": (_i, [_p, _p, _f, _i64, _i64, _p, _p]),

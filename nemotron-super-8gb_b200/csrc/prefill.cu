@@ -108,8 +108,9 @@ struct Params {
 };
 
 // ------------------------------------------------------------------------------------------ routing
-// Per chunk of CHUNK_T tokens: histogram of expert ids. An id outside [0, ne) is recorded as a shape
-// error and its pair dropped (its (t, k) slot then yields NaN in the combine).
+// Per chunk of CHUNK_T tokens: histogram of expert ids. Id -1 means "no expert" (an expert-parallel block
+// row whose expert lives on another rank): the pair is skipped and contributes nothing. Any other id outside
+// [0, ne) is recorded as a shape error and its pair dropped (its (t, k) slot then yields NaN in the combine).
 __global__ void __launch_bounds__(256) pf_hist_kernel(const Params p) {
     __shared__ int hist[MAX_NE];
     for (int e = threadIdx.x; e < p.ne; e += blockDim.x) hist[e] = 0;
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(256) pf_hist_kernel(const Params p) {
     const int n = (t1 - t0) * p.topk;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int e = p.ids[(int64_t)t0 * p.topk + i];
+        if (e == -1) continue;
         if (e < 0 || e >= p.ne) {
             set_error(p.status, QMOE_ERR_SHAPE);
             continue;
@@ -222,7 +224,7 @@ __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
             p.pair_coef[pos] = swt[(t - t0) * p.topk + lane];
             p.pair_pos[tk] = pos;
         } else if (valid) {
-            p.pair_pos[tk] = -1;
+            p.pair_pos[tk] = e == -1 ? -2 : -1;   // -2: no expert (skipped), -1: invalid id (NaN)
         }
         __syncwarp();
         if (ok && (mask & lt) == 0) base[e] += __popc(mask);
@@ -270,12 +272,13 @@ __global__ void __launch_bounds__(256) pf_gather_kernel(const Params p) {
     if (lane == 0) p.pair_exp[pr] = E;
 }
 
-// out[t] = sum over k (in order) of Op[pos(t, k)]; an invalid (t, k) contributes NaN.
+// out[t] = sum over k (in order) of Op[pos(t, k)]; an invalid (t, k) contributes NaN, a skipped one nothing.
 __global__ void __launch_bounds__(256) pf_combine_kernel(const Params p) {
     const int t = blockIdx.x;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < p.topk; k++) {
         const int pos = p.pair_pos[(int64_t)t * p.topk + k];
+        if (pos == -2) continue;
         float4 v;
         if (pos >= 0) {
             v = reinterpret_cast<const float4 *>(p.op + (int64_t)pos * LAT)[threadIdx.x];

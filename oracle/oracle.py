@@ -221,3 +221,61 @@ def cpu_layer_fp32(blocks, s2, coef, x, layoutT=False, nthreads=0):
 
 def max_threads():
     return int(lib().orc_max_threads())
+
+
+def prefill(blocks, s2, ids, w, X, layoutT=False):
+    """Prompt-path layer in fp64: out[t] = sum over k (in k order) of w[t,k] * s2[e,1] * D_e relu(s2[e,0] U_e x_t)^2,
+    e = ids[t,k]; ids of -1 are skipped (nem_super.py:336-348 with the pairs arithmetic of qmoe_ns.py:79-133)."""
+    ids = np.asarray(ids)
+    T, k = ids.shape
+    valid = ids >= 0
+    t_i, k_i = np.nonzero(valid)
+    out = np.zeros((T, LAT), dtype=np.float64)
+    if len(t_i) == 0:
+        return out
+    pslot = ids[t_i, k_i].astype(np.int32)
+    y = pairs(blocks, pslot, t_i.astype(np.int32), np.asarray(s2, np.float32)[pslot],
+              np.asarray(w, np.float32)[t_i, k_i], X, layoutT=layoutT)
+    Yd = np.zeros((T, k, LAT), dtype=np.float64)
+    Yd[t_i, k_i] = y
+    for kk in range(k):          # fixed k order
+        out += Yd[:, kk]
+    return out
+
+
+def ep_pack(x, ids, w, n_experts, world):
+    """Expert-parallel dispatch pack (no reference counterpart): expert e on rank e // (n_experts // world);
+    block d holds, in token order, the tokens with >= 1 expert on d: their x rows, block-local ids (-1 for
+    experts elsewhere and for unused rows) and weights. Returns send_x [world, T, ...], ids [world, T, k],
+    w [world, T, k], row_of [world, T] (-1: not in block d), cnt [world]."""
+    ids = np.asarray(ids)
+    T, k = ids.shape
+    el = n_experts // world
+    send_x = np.zeros((world,) + tuple(np.shape(x)), dtype=np.asarray(x).dtype)
+    s_ids = np.full((world, T, k), -1, dtype=np.int32)
+    s_w = np.zeros((world, T, k), dtype=np.float32)
+    row_of = np.full((world, T), -1, dtype=np.int32)
+    cnt = np.zeros(world, dtype=np.int32)
+    for d in range(world):
+        r = 0
+        for t in range(T):
+            loc = (ids[t] >= 0) & (ids[t] // el == d)
+            if loc.any():
+                send_x[d, r] = x[t]
+                s_ids[d, r] = np.where(loc, ids[t] - d * el, -1)
+                s_w[d, r] = w[t]
+                row_of[d, t] = r
+                r += 1
+        cnt[d] = r
+    return send_x, s_ids, s_w, row_of, cnt
+
+
+def ep_combine(part, row_of):
+    """out[t] = sum over ranks d in order of part[d, row_of[d, t]] (row_of -1 skipped)."""
+    world, T = row_of.shape
+    out = np.zeros((T,) + part.shape[2:], dtype=np.float64)
+    for d in range(world):
+        for t in range(T):
+            if row_of[d, t] >= 0:
+                out[t] += part[d, row_of[d, t]]
+    return out
