@@ -171,6 +171,11 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
+// Hint: bring the 128-byte line at p into L2, kept with evict_last priority.
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
 // Record the first device-side error in a status word.
 __device__ __forceinline__ void set_error(int *status, int code) {
     if (status) atomicCAS(status, 0, code);

@@ -41,6 +41,7 @@ struct UpArgs {
     int *status;        // device status word (nullable)
     int *zero_words;    // words zeroed for the dependent kernel (nullable)
     int nzero;
+    const int64_t *tab; // T-layout blocks the down kernel reads (nullable): live rows are prefetched to L2
 };
 
 struct UpTile {      // one lane's share of an 8-row tile: 16 B of codes and 2 scale bytes per row
@@ -68,12 +69,17 @@ __device__ __forceinline__ void up_load(const uint8_t *base, int hg, int lane, U
 __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
     __shared__ const uint8_t *s_base[UP_MAXK];   // slot base of expert j (nullptr: slot out of range)
     __shared__ float s_s2u[UP_MAXK];
+    __shared__ const uint8_t *s_tab[UP_MAXK];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = a.K * UP_HALVES;
+    // Launched as a programmatic dependent of the previous layer's kernels: everything below may read their
+    // outputs (sidx, x) or rewrite buffers they still read (the workspace counters), so wait first.
+    pdl_wait();
     for (int j = threadIdx.x; j < a.K && j < UP_MAXK; j += blockDim.x) {
         const int64_t slot = a.sidx[j];
         s_base[j] = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
         s_s2u[j] = a.s2[2 * j];
+        s_tab[j] = a.tab ? reinterpret_cast<const uint8_t *>(a.tab[j]) : nullptr;
     }
     if (blockIdx.x == 0 && a.zero_words && (int)threadIdx.x < a.nzero) a.zero_words[threadIdx.x] = 0;
     __syncthreads();
@@ -183,9 +189,20 @@ __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
         if (bad) hv = __int_as_float(0x7fc00000);
         const bool lead = (lane & 3) == 0;
         if (lead) a.h[(int64_t)j * INTER + hg * UP_ROWS + (lane >> 2)] = hv;
-        if (a.gmask8) {
+        if (a.gmask8 || a.tab) {
             const unsigned m = __reduce_or_sync(0xffffffffu, (lead && (hv > 0.f || bad)) ? (1u << (lane >> 2)) : 0u);
-            if (lane == 0) a.gmask8[(int64_t)j * UP_HALVES + hg] = (uint8_t)m;
+            if (a.gmask8 && lane == 0) a.gmask8[(int64_t)j * UP_HALVES + hg] = (uint8_t)m;
+            // The down kernel reads, per live neuron, its 512-byte row of dnT_w and, per live group, the
+            // group's 1024-byte row of dnT_s: start bringing them into L2 now, while the up stream runs.
+            const uint8_t *tb = a.tab ? (j < UP_MAXK ? s_tab[j] : reinterpret_cast<const uint8_t *>(a.tab[j])) : nullptr;
+            if (tb && !bad && m) {
+                if (lead && hv > 0.f) {
+                    const uint8_t *row = tb + O_DW + (int64_t)(hg * UP_ROWS + (lane >> 2)) * (LAT / 2);
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) prefetch_l2(row + 128 * l);
+                }
+                if (lane >= 24) prefetch_l2(tb + O_DS + (int64_t)(hg >> 1) * LAT + 128 * (lane - 24));
+            }
         }
     }
 }
@@ -264,6 +281,7 @@ __global__ void __launch_bounds__(DN_THREADS) decode_down_kernel(DownArgs a) {
     const bool bad = (reinterpret_cast<uintptr_t>(blk) & 15u) != 0 || blk == nullptr;
     const float cmul = a.coef[j] * a.s2[2 * j + 1];
 
+    pdl_launch_dependents();   // the next kernel (the next layer's up) may start its launch now
     pdl_wait();  // the up kernel's h and masks are complete and visible
 
     // ---- 1. live neurons of this CTA's groups, ascending: thread t < 168 takes the t-th listed group;
@@ -425,10 +443,23 @@ __global__ void sum_rows_kernel(const float *__restrict__ out, int K, float *__r
 // ------------------------------------------------------------------ host launchers
 static std::atomic<uint64_t> g_dn_smem_f{0}, g_dn_smem_r{0};
 
+// The up kernel is launched as a programmatic dependent of whatever precedes it on the stream (for a decode
+// step, the previous layer's down kernel): its CTAs are resident and waiting in griddepcontrol.wait when
+// that kernel finishes, instead of being launched only then.
 static int launch_up(const UpArgs &a, cudaStream_t st, int dev, const DeviceInfo &di) {
+    (void)dev;
     const int ntiles = a.K * UP_HALVES;
-    const int grid = ntiles < di.sms ? ntiles : di.sms;
-    decode_up_kernel<<<grid, UP_THREADS, 0, st>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ntiles < di.sms ? ntiles : di.sms);
+    cfg.blockDim = dim3(UP_THREADS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, decode_up_kernel, a) != cudaSuccess) return QMOE_ERR_LAUNCH;
     return launch_status();
 }
 
@@ -537,7 +568,7 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
     int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);
     uint8_t *gmask8 = ws + WS_GMASK;
     cudaStream_t st = as_stream(stream);
-    UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK};
+    UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
     return launch_down<true>(da, st, dev, true);
@@ -642,7 +673,7 @@ int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64
     int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);   // zeroed by the up kernel on every call
     uint8_t *gmask8 = ws + WS_GMASK;                              // rewritten in full on every call
     cudaStream_t st = as_stream(stream);
-    UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK};
+    UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
     return launch_down<true>(da, st, dev, true);
