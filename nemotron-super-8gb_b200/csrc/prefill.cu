@@ -105,6 +105,9 @@ struct Params {
     __half *xp;             // [P, 1024]
     __half *hs;             // [P, 2688]
     float *op;              // [P, 1024]
+    int *pair_tile;         // [P] tile of each sorted pair
+    uint8_t *xq, *xsc;      // [NP, P, 512] e2m1 codes, [NP, P, 64] e4m3 scales: x as NVFP4 residual planes
+    uint8_t *hq, *hsc;      // [NP, P, 1344], [NP, P, 168]: h (x 2^S0 of its tile) as NVFP4 residual planes
 };
 
 // ------------------------------------------------------------------------------------------ routing
@@ -187,6 +190,7 @@ __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
             const int n0 = off + i * NT;
             p.tiles[toff + i] = make_int4(e, n0, min(NT, cnt - i * NT), 0);
         }
+        for (int i = 0; i < cnt; i++) p.pair_tile[off + i] = toff + i / NT;
     }
     if (threadIdx.x == blockDim.x - 1) {
         p.eoff[p.ne] = warp_sum[0][31];
@@ -230,46 +234,6 @@ __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
         if (ok && (mask & lt) == 0) base[e] += __popc(mask);
         __syncwarp();
     }
-}
-
-// One warp per sorted pair: Xp[p] = f16(x[t] * 2^E), E from the token's amax (exact for bf16 input).
-__global__ void __launch_bounds__(256) pf_gather_kernel(const Params p) {
-    const int lane = threadIdx.x & 31;
-    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (pr >= p.eoff[p.ne]) return;
-    const int t = p.pair_tok[pr];
-    float v[32];
-    if (p.x_dtype == QMOE_DT_BF16) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) +
-                                                          (int64_t)t * LAT + lane * 32);
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint4 w = src[i];
-            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                v[i * 8 + 2 * j] = __uint_as_float(u[j] << 16);
-                v[i * 8 + 2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
-            }
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = load_act(p.x, p.x_dtype, (int64_t)t * LAT + lane * 32 + i);
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const int E = prescale_exp(amax, 15);
-    const float sc = pow2f(E);
-    uint32_t o[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) o[i] = h2_as_u(__floats2half2_rn(v[2 * i] * sc, v[2 * i + 1] * sc));
-    uint4 *dst = reinterpret_cast<uint4 *>(p.xp + (int64_t)pr * LAT + lane * 32);
-#pragma unroll
-    for (int i = 0; i < 4; i++) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-    if (lane == 0) p.pair_exp[pr] = E;
 }
 
 // out[t] = sum over k (in order) of Op[pos(t, k)]; an invalid (t, k) contributes NaN, a skipped one nothing.
@@ -807,10 +771,469 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------ block-scaled
+// The NVFP4 block-scaled path: tcgen05.mma.kind::mxf4nvf4.block_scale.block16 takes the weights exactly as
+// stored (e2m1 codes, one e4m3 scale per 16 along k, K-major: up_w and the orig-layout dn_w) straight from
+// TMA, with no decode. The other operand, the pairs' activations, is given as NP "residual planes": plane 0
+// is the NVFP4 quantization of the row (per-16 e4m3 scale = amax/6), plane p+1 quantizes what plane p left
+// over, so the sum of the planes is the row to ~amax/6^NP per 16-element group (measured output rel-L2
+// ~8e-4 for x and ~2e-4 for h at NP = 3). Each k-step of 64 is NP MMAs into one fp32 accumulator.
+constexpr int NP = 3;                    // activation planes
+constexpr int HSHIFT = 4;                // h planes carry h * 2^(S0 - HSHIFT): block amax <= 2^11, scale <= 2^11 / 6
+constexpr int BS_BK = 128;               // k per stage: two MMA k-steps of 64
+constexpr int BS_KS = BS_BK / 64;        // MMA k-steps per stage
+constexpr int BS_STAGES = 5;
+constexpr int BS_A = BM * BS_BK / 2;     // 8 KB: 128 weight rows x 64 B, 64-byte swizzle
+constexpr int BS_B = NP * NT * BS_BK / 2;   // 24 KB: NP planes x up to 128 pair rows x 64 B
+constexpr int BS_ATOM = 512;             // scale-factor atom: 128 rows x 4 scales, byte (r%32)*16 + (r/32)*4 + k
+constexpr int BS_SF = BS_KS * (1 + NP) * BS_ATOM;   // SFA + NP SFB atoms per k-step
+constexpr int BS_STAGE = BS_A + BS_B + BS_SF;
+constexpr int BS_OFF_STG = BS_STAGES * BS_STAGE;
+constexpr int BS_OFF_COLSC = BS_OFF_STG + STG_COLS * BM * 2;
+constexpr int BS_OFF_RED = BS_OFF_COLSC + 2 * NT * 4;
+constexpr int BS_OFF_BAR = BS_OFF_RED + 32;
+constexpr int BS_NBAR = 2 * BS_STAGES + 4;
+constexpr int BS_OFF_TMEM = BS_OFF_BAR + BS_NBAR * 8;
+constexpr int BS_OFF_ABORT = BS_OFF_TMEM + 16;
+constexpr int BS_SMEM = BS_OFF_ABORT + 16 + 1024;
+static_assert(BS_SMEM <= 232448, "fits the 227 KB opt-in");
+static_assert(BS_STAGE % 1024 == 0 && BS_A % 512 == 0, "TMA destinations and swizzle atoms");
+constexpr int BS_NA = 2, BS_NB = 2, BS_NSF = 2;       // A issuers, B issuers, scale-factor loader warps
+constexpr int BS_W_A = 4, BS_W_B = BS_W_A + BS_NA, BS_W_SF = BS_W_B + BS_NB, BS_W_MMA = BS_W_SF + BS_NSF;
+constexpr int BS_THREADS = (BS_W_MMA + 1) * 32;
+constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and NT; scale factors from 2*NT
+constexpr int BS_SF_COL = 2 * NT;
+
+// Pair rows loaded for a tile of n pairs (the TMA box heights).
+__device__ __forceinline__ int b_rows(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
+
+// 16 fp32 values -> NP NVFP4 planes: codes[p] = 8 bytes (element 2i in the low nibble of byte i), scale
+// byte sc[p] (e4m3, round to nearest; the e2m1 codes saturate, the residual carries the difference).
+__device__ __forceinline__ void nvfp4_planes16(float (&v)[16], uint32_t (&codes)[NP][2], uint8_t (&sc)[NP]) {
+#pragma unroll
+    for (int pl = 0; pl < NP; ++pl) {
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        uint32_t s16;
+        asm("{\n\t.reg .b16 t;\n\tcvt.rn.satfinite.e4m3x2.f32 t, %1, %2;\n\tcvt.u32.u16 %0, t;\n\t}"
+            : "=r"(s16) : "f"(0.f), "f"(amax * (1.f / 6.f)));
+        const uint8_t sb = (uint8_t)(s16 & 0xFFu);
+        const float s = e4m3_f32(sb);
+        sc[pl] = sb;
+        codes[pl][0] = codes[pl][1] = 0u;
+        if (!(s > 0.f)) continue;
+        const float inv = 1.f / s;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            uint32_t b;
+            asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
+                : "=r"(b) : "f"(v[2 * i + 1] * inv), "f"(v[2 * i] * inv));
+            codes[pl][i >> 2] |= b << (8 * (i & 3));
+            uint32_t h2;
+            asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(b));
+            const float2 q = __half22float2(as_h2(h2));   // (element 2i, element 2i+1)
+            v[2 * i] -= q.x * s;
+            v[2 * i + 1] -= q.y * s;
+        }
+    }
+}
+
+// One warp per sorted pair: x[token] * 2^E (amax in [2^8, 2^9)) as NP planes; E per pair for the epilogue.
+__global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pr >= p.eoff[p.ne]) return;
+    const int t = p.pair_tok[pr];
+    float v[32];
+    if (p.x_dtype == QMOE_DT_BF16) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) +
+                                                          (int64_t)t * LAT + lane * 32);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 w = src[i];
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                v[i * 8 + 2 * j] = __uint_as_float(u[j] << 16);
+                v[i * 8 + 2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = load_act(p.x, p.x_dtype, (int64_t)t * LAT + lane * 32 + i);
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const int E = prescale_exp(amax, 9);
+    const float scl = pow2f(E);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {   // groups 2*lane, 2*lane+1 of the row
+        float w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = v[16 * g + i] * scl;
+        uint32_t codes[NP][2];
+        uint8_t sc[NP];
+        nvfp4_planes16(w, codes, sc);
+        const int grp = 2 * lane + g;
+#pragma unroll
+        for (int pl = 0; pl < NP; ++pl) {
+            *reinterpret_cast<uint2 *>(p.xq + ((int64_t)pl * p.P + pr) * (LAT / 2) + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
+            p.xsc[((int64_t)pl * p.P + pr) * G_UP + grp] = sc[pl];
+        }
+    }
+    if (lane == 0) p.pair_exp[pr] = E;
+}
+
+// One warp per sorted pair: its h row (f16, block b scaled by 2^S_b of its tile) times 2^(S0 - HSHIFT - S_b),
+// S0 the tile's smallest block exponent, as NP planes: the planes carry h * 2^(S0 - HSHIFT) for the whole row
+// (the largest block amax lands in [2^10, 2^11), inside the e4m3 range of the plane scales).
+__global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pr >= p.eoff[p.ne]) return;
+    const int tile = p.pair_tile[pr];
+    const int sb_l = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
+    int s0 = sb_l;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
+    for (int g0 = 0; g0 < G_DN; g0 += 32) {
+        const int grp = g0 + lane;
+        const int blkid = (grp < G_DN ? grp : G_DN - 1) >> 3;
+        const int sbk = __shfl_sync(0xffffffffu, sb_l, blkid);
+        if (grp >= G_DN) continue;
+        const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
+        const float f = d >= -126 ? pow2f(d) : 0.f;
+        const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
+        const uint4 a = src[0], b = src[1];
+        const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        float w[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float2 q = __half22float2(as_h2(u[i]));
+            w[2 * i] = q.x * f;
+            w[2 * i + 1] = q.y * f;
+        }
+        uint32_t codes[NP][2];
+        uint8_t sc[NP];
+        nvfp4_planes16(w, codes, sc);
+#pragma unroll
+        for (int pl = 0; pl < NP; ++pl) {
+            *reinterpret_cast<uint2 *>(p.hq + ((int64_t)pl * p.P + pr) * KB_DN + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
+            p.hsc[((int64_t)pl * p.P + pr) * G_DN + grp] = sc[pl];
+        }
+    }
+}
+
+__device__ __forceinline__ void mma_nvfp4(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc,
+                                          uint32_t tsfa, uint32_t tsfb) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(tsfa), "r"(tsfb)
+        : "memory");
+}
+
+// Scale-factor atom (128 rows x 4 e4m3, the layout above) from shared memory into 4 TMEM columns of all
+// 128 lanes (the 32-row pattern is broadcast to the four lane quarters).
+__device__ __forceinline__ void tmem_cp_sf(uint32_t tmem_col, uint32_t atom_addr) {
+    const uint64_t d = smem_desc(atom_addr, 16, 128, 0);
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(d) : "memory");
+}
+
+// Instruction descriptor of kind::mxf4nvf4: A, B e2m1 (format 1), K-major, e4m3 scales, M = 128, N = n, K = 64.
+__device__ __forceinline__ uint32_t instr_desc_nvfp4(int n) {
+    return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// The grouped GEMM on block-scaled NVFP4 MMA; persistent, items (tile, 128 weight rows) as pf_gemm_kernel.
+// Roles: warps 4..5 load the weight stages (TMA, 8 KB, 64-byte swizzle), warps 6..7 the NP activation planes
+// of the stage (one 3-D TMA box: planes x pair rows x 64 B), warps 8..9 assemble the scale-factor atoms with
+// 4-byte cp.async; warp 10 copies the atoms into TMEM and issues NP MMAs per k-step; warps 0..3 drain the
+// other accumulator (epilogue as pf_gemm_kernel).
+template <int PH>
+__global__ void __launch_bounds__(BS_THREADS, 1)
+    pfb_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b16,
+                    const __grid_constant__ CUtensorMap tm_b32, const __grid_constant__ CUtensorMap tm_b64,
+                    const __grid_constant__ CUtensorMap tm_b128) {
+    constexpr int MT = PH == PH_UP ? MT_UP : MT_DN;
+    constexpr int K = PH == PH_UP ? LAT : INTER;
+    constexpr int NST = K / BS_BK;                     // stages per item
+    constexpr int GP = PH == PH_UP ? G_UP : G_DN;      // scale bytes per row (weights and planes)
+    const int nitems = *p.tile_count * MT;
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_base = smem_u32(smem_raw);
+    uint8_t *sm = smem_raw + (((raw_base + 1023u) & ~1023u) - raw_base);
+    const uint32_t sbase = smem_u32(sm);
+    float *colsc = reinterpret_cast<float *>(sm + BS_OFF_COLSC);
+    float *red = reinterpret_cast<float *>(sm + BS_OFF_RED);
+    __half *stg = reinterpret_cast<__half *>(sm + BS_OFF_STG);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + BS_OFF_BAR);
+    uint64_t *empty = full + BS_STAGES;
+    uint64_t *acc_full = empty + BS_STAGES;
+    uint64_t *acc_empty = acc_full + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + BS_OFF_TMEM);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + BS_OFF_ABORT);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        for (int s = 0; s < BS_STAGES; s++) {
+            mbar_init(&full[s], 2 + BS_NSF * 32);   // A and B expect_tx arrivals + one per scale loader thread
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 4);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == BS_W_MMA) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(BS_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp >= BS_W_A && warp < BS_W_B) {
+        // ------------------------------------------------------------ weights: codes [128 rows][64 B] per stage
+        const int pr = warp - BS_W_A;
+        if (lane == 0) {
+            uint32_t q = 0;
+            int e_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].x : 0;
+            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
+                const int mt = i % MT, e = e_next;
+                if (i + (int)gridDim.x < nitems) e_next = p.tiles[(i + gridDim.x) / MT].x;
+                bool ok = true;
+                for (int kt = 0; kt < NST; kt++, q++) {
+                    if ((int)(q % BS_NA) != pr) continue;
+                    const int s = q % BS_STAGES;
+                    if (!lane_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], BS_A);
+                    tma_load_3d(sm + s * BS_STAGE, &tm_w, kt * (BS_BK / 2), (PH == PH_UP ? 0 : ROW1344_DW) + mt * BM, e,
+                                &full[s]);
+                }
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else if (warp >= BS_W_B && warp < BS_W_SF) {
+        // ------------------------------------------------------------ activation planes [NP][rows][64 B] per stage
+        const int pb = warp - BS_W_B;
+        if (lane == 0) {
+            uint32_t q = 0;
+            int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
+            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
+                const int4 td = td_next;
+                if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
+                const int n0 = td.y, np_ = b_rows(td.z);
+                const CUtensorMap *map = np_ == 16 ? &tm_b16 : np_ == 32 ? &tm_b32 : np_ == 64 ? &tm_b64 : &tm_b128;
+                bool ok = true;
+                for (int kt = 0; kt < NST; kt++, q++) {
+                    if ((int)(q % BS_NB) != pb) continue;
+                    const int s = q % BS_STAGES;
+                    if (!lane_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2)));
+                    tma_load_3d(sm + s * BS_STAGE + BS_A, map, kt * (BS_BK / 2), n0, 0, &full[s]);
+                }
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else if (warp >= BS_W_SF && warp < BS_W_MMA) {
+        // ------------------------------------------------------------ scale-factor atoms by 4-byte cp.async
+        const int st = tid - BS_W_SF * 32;   // 0 .. 63
+        const uint8_t *psc = PH == PH_UP ? p.xsc : p.hsc;
+        uint32_t q = 0;
+        int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
+        for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
+            const int4 td = td_next;
+            if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
+            const int e = td.x, n0 = td.y, n = td.z, mt = i % MT;
+            const uint8_t *wsc = p.store + (int64_t)e * p.bstride + (PH == PH_UP ? O_US : O_DS) + (int64_t)mt * BM * GP;
+            bool ok = true;
+            for (int kt = 0; kt < NST; kt++, q++) {
+                const int s = q % BS_STAGES;
+                if (!warp_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, lane, abort_flag, p.status)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t sf = sbase + s * BS_STAGE + BS_A + BS_B;
+                const int per = BM + NP * n;   // rows of one k-step: weight rows, then the planes' pair rows
+                for (int w = st; w < BS_KS * per; w += BS_NSF * 32) {
+                    const int kk = w / per, rr = w - kk * per;
+                    const int ks = kt * BS_KS + kk;   // k-step: scale bytes 4ks .. 4ks+3 of the row
+                    const uint8_t *src;
+                    int row, atom;
+                    if (rr < BM) {
+                        row = rr;
+                        atom = kk * (1 + NP);
+                        src = wsc + (int64_t)row * GP + 4 * ks;
+                    } else {
+                        const int pl = (rr - BM) / n;
+                        row = (rr - BM) - pl * n;
+                        atom = kk * (1 + NP) + 1 + pl;
+                        src = psc + ((int64_t)pl * p.P + n0 + row) * GP + 4 * ks;
+                    }
+                    const uint32_t dst = sf + atom * BS_ATOM + (row & 31) * 16 + (row >> 5) * 4;
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+                }
+                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
+            }
+            if (!ok) break;
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+    } else if (warp == BS_W_MMA) {
+        // ------------------------------------------------------------ scale factors -> TMEM, NP MMAs per k-step
+        if (lane == 0) {
+            uint32_t q = 0;
+            int n_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].z : 0;
+            for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
+                const int n = n_next;
+                if (i + (int)gridDim.x < nitems) n_next = p.tiles[(i + gridDim.x) / MT].z;
+                const int np_ = b_rows(n);
+                const int a = j & 1;
+                if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+                tc_fence_after();
+                const uint32_t idesc = instr_desc_nvfp4((n + 15) & ~15);
+                const uint32_t d = tmem + a * NT;
+                bool ok = true;
+                for (int kt = 0; kt < NST; kt++, q++) {
+                    const int s = q % BS_STAGES;
+                    if (!lane_wait(&full[s], (q / BS_STAGES) & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    fence_async_smem();   // the cp.async-written scale atoms -> visible to the async proxy
+                    tc_fence_after();
+                    const uint32_t st0 = sbase + s * BS_STAGE;
+#pragma unroll
+                    for (int kk = 0; kk < BS_KS; kk++) {
+                        const uint32_t sfa = tmem + BS_SF_COL + kk * 16;   // 4 columns SFA, then 4 per plane
+                        const uint32_t atoms = st0 + BS_A + BS_B + kk * (1 + NP) * BS_ATOM;
+                        tmem_cp_sf(sfa, atoms);
+#pragma unroll
+                        for (int pl = 0; pl < NP; pl++) tmem_cp_sf(sfa + 4 + 4 * pl, atoms + (1 + pl) * BS_ATOM);
+                        const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
+#pragma unroll
+                        for (int pl = 0; pl < NP; pl++) {
+                            const uint64_t bd = smem_desc(st0 + BS_A + pl * np_ * (BS_BK / 2) + kk * 32, 16, 512, 4);
+                            mma_nvfp4(d, ad, bd, idesc, (kt | kk | pl) != 0, sfa, sfa + 4 + 4 * pl);
+                        }
+                    }
+                    mma_commit(&empty[s]);
+                }
+                mma_commit(&acc_full[a]);   // also after a failed wait: tracks every MMA issued
+                if (!ok) break;
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 0..3 = TMEM lanes)
+        const int m = tid;
+        for (int i = blockIdx.x, j = 0; i < nitems; i += gridDim.x, j++) {
+            const int tile = i / MT, mt = i % MT;
+            const int4 td = p.tiles[tile];
+            const int e = td.x, n0 = td.y, n = td.z;
+            const int a = j & 1;
+            float *cs = colsc + a * NT;
+            const int s0 = PH != PH_UP ? tile_s0(p, tile, lane) : 0;
+            for (int jj = tid; jj < n; jj += 128) {
+                if (PH == PH_UP) cs[jj] = pow2f(-p.pair_exp[n0 + jj]) * p.s2[(int64_t)e * 2];
+                else cs[jj] = p.pair_coef[n0 + jj] * p.s2[(int64_t)e * 2 + 1] * pow2f(min(HSHIFT - s0, 127));
+            }
+            named_sync(1, 128);
+            const bool acc_ok = warp_wait(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
+            tc_fence_after();
+            const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
+            if (PH == PH_UP) {
+                float mx = 0.f;
+                if (acc_ok) {
+                    for (int c0 = 0; c0 < n; c0 += 32) {
+                        float v[32];
+                        tmem_ld32(trow + c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj++) {
+                            if (c0 + jj < n) {
+                                const float u = v[jj] * cs[c0 + jj];
+                                mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (lane == 0) red[a * 4 + warp] = mx;
+                named_sync(1, 128);
+                mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
+                const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
+                if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
+                const float sc = pow2f(S);
+                for (int c0 = 0; c0 < n; c0 += STG_COLS) {
+                    if (acc_ok) {
+                        float v[16];
+                        tmem_ld16(trow + c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < STG_COLS; jj++) {
+                            const float u = v[jj] * cs[(c0 + jj) & (NT - 1)];
+                            stg[jj * BM + m] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
+                        }
+                    }
+                    named_sync(1, 128);
+                    if (acc_ok) {
+#pragma unroll
+                        for (int k2 = 0; k2 < 2; k2++) {
+                            const int piece = tid + 128 * k2;
+                            const int row = piece >> 4, part = piece & 15;
+                            if (c0 + row < n)
+                                *reinterpret_cast<uint4 *>(p.hs + (int64_t)(n0 + c0 + row) * INTER + mt * BM + part * 8) =
+                                    *reinterpret_cast<const uint4 *>(stg + row * BM + part * 8);
+                        }
+                    }
+                    named_sync(1, 128);
+                }
+            } else if (acc_ok) {
+                float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
+                for (int c0 = 0; c0 < n; c0 += 32) {
+                    float v[32];
+                    tmem_ld32(trow + c0, v);
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj++)
+                        if (c0 + jj < n) dst[(int64_t)(c0 + jj) * LAT] = v[jj] * cs[c0 + jj];
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == BS_W_MMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BS_TMEM_COLS) : "memory");
+    }
+}
+
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
     size_t status, tile_count, cnt, eoff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
-        xp, hs, op, total;
+        hs, op, pair_tile, xq, xsc, hq, hsc, total;
     int P, nchunks, tiles_cap;
 };
 
@@ -838,9 +1261,13 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.pair_pos = take(sizeof(int) * (size_t)L.P);
     L.pair_exp = take(sizeof(int) * (size_t)L.P);
     L.tile_scale = take(sizeof(int) * (size_t)L.tiles_cap * MT_UP);
-    L.xp = take((size_t)L.P * LAT * 2);
     L.hs = take((size_t)L.P * INTER * 2);
     L.op = take((size_t)L.P * LAT * 4);
+    L.pair_tile = take(sizeof(int) * (size_t)L.P);
+    L.xq = take((size_t)NP * L.P * (LAT / 2));
+    L.xsc = take((size_t)NP * L.P * G_UP);
+    L.hq = take((size_t)NP * L.P * KB_DN);
+    L.hsc = take((size_t)NP * L.P * G_DN);
     L.total = o;
     return L;
 }
@@ -878,7 +1305,7 @@ inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int
 // The store as a u8 tensor [ne][BLOCK / pitch][pitch] (expert stride bstride), for TMA boxes of
 // {box_x bytes, box_y rows} out of one block region.
 inline bool make_store_map(CUtensorMap *m, const void *store, int64_t bstride, int ne, int pitch, int box_x,
-                           int box_y) {
+                           int box_y, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return false;
     const cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)(BLOCK / pitch), (cuuint64_t)ne};
@@ -886,8 +1313,21 @@ inline bool make_store_map(CUtensorMap *m, const void *store, int64_t bstride, i
     const cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)box_y, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(store), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// NVFP4 planes [NP][P][row_bytes] u8 -> map with boxes {64 B, box_rows, NP} and 64-byte swizzle (rows past P
+// read as zero).
+inline bool make_plane_map(CUtensorMap *m, void *base, int64_t P, int row_bytes, int box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {(cuuint64_t)row_bytes, (cuuint64_t)P, (cuuint64_t)NP};
+    const cuuint64_t strides[2] = {(cuuint64_t)row_bytes, (cuuint64_t)P * row_bytes};
+    const cuuint32_t box[3] = {(cuuint32_t)(BS_BK / 2), (cuuint32_t)box_rows, (cuuint32_t)NP};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 std::atomic<uint64_t> g_smem_up{0}, g_smem_dn_t{0}, g_smem_dn_o{0};
@@ -949,31 +1389,51 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.pair_pos = reinterpret_cast<int *>(ws + L.pair_pos);
     p.pair_exp = reinterpret_cast<int *>(ws + L.pair_exp);
     p.tile_scale = reinterpret_cast<int *>(ws + L.tile_scale);
-    p.xp = reinterpret_cast<__half *>(ws + L.xp);
+    p.xp = nullptr;
     p.hs = reinterpret_cast<__half *>(ws + L.hs);
     p.op = reinterpret_cast<float *>(ws + L.op);
+    p.pair_tile = reinterpret_cast<int *>(ws + L.pair_tile);
+    p.xq = ws + L.xq;
+    p.xsc = ws + L.xsc;
+    p.hq = ws + L.hq;
+    p.hsc = ws + L.hsc;
 
-    CUtensorMap bx[4], bh[4], wu, wd, sd;
+    // up: block-scaled NVFP4 (weights as stored, x as NVFP4 planes); down: block-scaled on the orig layout,
+    // or the exact-f16 kernel on the T layout (FP4 operands of the tensor core must be K-major)
     const int hts[4] = {16, 32, 64, 128};
-    for (int k = 0; k < 4; k++)
-        if (!make_map(&bx[k], p.xp, L.P, LAT, hts[k]) || !make_map(&bh[k], p.hs, L.P, INTER, hts[k])) return QMOE_ERR_LAUNCH;
-    if (!make_store_map(&wu, store, block_stride, n_experts, 512, RK / 2, BM) ||
-        !make_store_map(&wd, store, block_stride, n_experts, layout_T ? 512 : 1344, layout_T ? BM / 2 : RK / 2,
-                        layout_T ? RK : BM) ||
-        !make_store_map(&sd, store, block_stride, n_experts, 1024, BM, G_DN))
+    CUtensorMap xm[4], hm[4], bh[4], wu, wdo, wdt, sdt;
+    for (int k = 0; k < 4; k++) {
+        if (!make_plane_map(&xm[k], p.xq, L.P, LAT / 2, hts[k])) return QMOE_ERR_LAUNCH;
+        if (layout_T ? !make_map(&bh[k], p.hs, L.P, INTER, hts[k]) : !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
+            return QMOE_ERR_LAUNCH;
+    }
+    if (!make_store_map(&wu, store, block_stride, n_experts, KB_UP, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;
-    auto up = pf_gemm_kernel<PH_UP>;
-    auto dn = layout_T ? pf_gemm_kernel<PH_DN_T> : pf_gemm_kernel<PH_DN_O>;
-    if (!ensure_smem(up, SMEM_BYTES, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
-    if (!ensure_smem(dn, SMEM_BYTES, dev, layout_T ? g_smem_dn_t : g_smem_dn_o)) return QMOE_ERR_LAUNCH;
+    if (layout_T) {
+        if (!make_store_map(&wdt, store, block_stride, n_experts, 512, BM / 2, RK) ||
+            !make_store_map(&sdt, store, block_stride, n_experts, 1024, BM, G_DN))
+            return QMOE_ERR_LAUNCH;
+    } else if (!make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B)) {
+        return QMOE_ERR_LAUNCH;
+    }
+    auto up = pfb_gemm_kernel<PH_UP>;
+    if (!ensure_smem(up, BS_SMEM, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
+    if (layout_T ? !ensure_smem(pf_gemm_kernel<PH_DN_T>, SMEM_BYTES, dev, g_smem_dn_t)
+                 : !ensure_smem(pfb_gemm_kernel<PH_DN_O>, BS_SMEM, dev, g_smem_dn_o))
+        return QMOE_ERR_LAUNCH;
 
     cudaStream_t st = as_stream(stream);
     pf_hist_kernel<<<L.nchunks, 256, 0, st>>>(p);
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
-    pf_gather_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-    up<<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bx[0], bx[1], bx[2], bx[3], wu, wu, wu);
-    dn<<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wd, wd, sd);
+    pf_xplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
+    up<<<di->sms, BS_THREADS, BS_SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
+    if (layout_T) {
+        pf_gemm_kernel<PH_DN_T><<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wdt, wdt, sdt);
+    } else {
+        pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
+        pfb_gemm_kernel<PH_DN_O><<<di->sms, BS_THREADS, BS_SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
+    }
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
 }

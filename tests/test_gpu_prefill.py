@@ -2,9 +2,9 @@
 qmoe_ns.moe_prefill, against the fp64 oracle of moe_pairs (qmoe_ns.py:79-133) combined over top-k in k
 order (nem_super.py:309-347), and against the reference's own moe_pairs golden vector.
 
-Bars: rel-L2 <= 2^-8 (BF16_TOL) of the fp64 oracle for every token (the only roundings are fp32
-accumulation and the f16 storage of h, ~1e-4); deterministic bit-identical reruns; the T and orig
-layouts agree; an invalid expert id is reported and poisons only its own token.
+Bars: rel-L2 <= 2^-8 (BF16_TOL) of the fp64 oracle for every token (the activations enter the block-scaled
+NVFP4 MMA as three NVFP4 residual planes, ~8e-4; h is stored as f16); deterministic bit-identical reruns;
+the T and orig layouts agree; an invalid expert id is reported and poisons only its own token.
 """
 import numpy as np
 import pytest
@@ -84,7 +84,9 @@ def test_prefill_golden_pairs(Q, golden):
     Q.to_T_batch(storeT)
     yT = Q.moe_prefill(storeT, torch.from_numpy(ids).to(DEV), torch.from_numpy(w).to(DEV),
                        torch.from_numpy(s2).to(DEV), Xd, layout_T=True)
-    assert rel_l2(yT.cpu().numpy(), y.cpu().numpy()) < 1e-6
+    # the T layout's down half runs the exact-f16 kernel, the orig layout's the block-scaled one
+    assert rel_l2(yT.cpu().numpy(), ref) < BF16_TOL
+    assert rel_l2(yT.cpu().numpy(), y.cpu().numpy()) < 2e-3
 
 
 @pytest.mark.parametrize("T,k", [(1, 1), (1, 22), (37, 8), (48, 22)])
@@ -137,7 +139,7 @@ def test_prefill_deterministic_and_matches_decode(Q, bank):
                                  b["X"][t], torch.empty(k, 2688, device=DEV), torch.empty(2, k, 1024, device=DEV),
                                  torch.empty(k, 168, dtype=torch.int32, device=DEV),
                                  torch.empty(k, dtype=torch.int32, device=DEV))
-        assert rel_l2(y1[t].cpu().numpy(), yd.cpu().numpy()) < 1e-3
+        assert rel_l2(y1[t].cpu().numpy(), yd.cpu().numpy()) < BF16_TOL
 
 
 def test_prefill_invalid_id_poisons_only_its_token(Q, bank):
