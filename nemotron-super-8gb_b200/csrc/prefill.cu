@@ -106,8 +106,8 @@ struct Params {
     __half *hs;             // [P, 2688]
     float *op;              // [P, 1024]
     int *pair_tile;         // [P] tile of each sorted pair
-    uint8_t *xq, *xsc;      // [NP, P, 512] e2m1 codes, [NP, P, 64] e4m3 scales: x as NVFP4 residual planes
-    uint8_t *hq, *hsc;      // [NP, P, 1344], [NP, P, 168]: h (x 2^S0 of its tile) as NVFP4 residual planes
+    uint8_t *xq, *hq;       // [NP, P, 512], [NP, P, 1344] e2m1 codes: x, h (x 2^S0 of its tile) as NVFP4 planes
+    uint8_t *sfbx, *sfbh;   // [tiles_cap, k-steps 16 | 42, NP, 512] the planes' e4m3 scales as tcgen05 atoms
 };
 
 // ------------------------------------------------------------------------------------------ routing
@@ -331,6 +331,14 @@ __device__ __forceinline__ uint32_t pow2_h2(int d) {
 }
 
 // 3-D tiled TMA load (box {x, y, 1}) into this CTA's shared memory, completing on `bar`.
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16), completing on bar.
+__device__ __forceinline__ void bulk_g2s_nohint(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
@@ -782,24 +790,36 @@ constexpr int NP = 3;                    // activation planes
 constexpr int HSHIFT = 4;                // h planes carry h * 2^(S0 - HSHIFT): block amax <= 2^11, scale <= 2^11 / 6
 constexpr int BS_BK = 128;               // k per stage: two MMA k-steps of 64
 constexpr int BS_KS = BS_BK / 64;        // MMA k-steps per stage
-constexpr int BS_STAGES = 5;
 constexpr int BS_A = BM * BS_BK / 2;     // 8 KB: 128 weight rows x 64 B, 64-byte swizzle
 constexpr int BS_B = NP * NT * BS_BK / 2;   // 24 KB: NP planes x up to 128 pair rows x 64 B
 constexpr int BS_ATOM = 512;             // scale-factor atom: 128 rows x 4 scales, byte (r%32)*16 + (r/32)*4 + k
-constexpr int BS_SF = BS_KS * (1 + NP) * BS_ATOM;   // SFA + NP SFB atoms per k-step
-constexpr int BS_STAGE = BS_A + BS_B + BS_SF;
-constexpr int BS_OFF_STG = BS_STAGES * BS_STAGE;
-constexpr int BS_OFF_COLSC = BS_OFF_STG + STG_COLS * BM * 2;
-constexpr int BS_OFF_RED = BS_OFF_COLSC + 2 * NT * 4;
-constexpr int BS_OFF_BAR = BS_OFF_RED + 32;
-constexpr int BS_NBAR = 2 * BS_STAGES + 4;
-constexpr int BS_OFF_TMEM = BS_OFF_BAR + BS_NBAR * 8;
-constexpr int BS_OFF_ABORT = BS_OFF_TMEM + 16;
-constexpr int BS_SMEM = BS_OFF_ABORT + 16 + 1024;
-static_assert(BS_SMEM <= 232448, "fits the 227 KB opt-in");
+constexpr int BS_SFB = BS_KS * NP * BS_ATOM;   // 3 KB: the planes' atoms of a stage, (k-step, plane) order
+constexpr int BS_SFA = BS_KS * BS_ATOM;        // 1 KB: the weights' atoms of a stage
+constexpr int BS_STAGE = BS_A + BS_B + BS_SFB + BS_SFA;
+constexpr int KS_UP = LAT / 64, KS_DN = INTER / 64;   // MMA k-steps of a row: 16 (up), 42 (down)
 static_assert(BS_STAGE % 1024 == 0 && BS_A % 512 == 0, "TMA destinations and swizzle atoms");
-constexpr int BS_NA = 2, BS_NB = 2, BS_NSF = 2;       // A issuers, B issuers, scale-factor loader warps
-constexpr int BS_W_A = 4, BS_W_B = BS_W_A + BS_NA, BS_W_SF = BS_W_B + BS_NB, BS_W_MMA = BS_W_SF + BS_NSF;
+
+// Shared-memory plan of pfb_gemm_kernel<PH>: the stage ring, two slabs of the item's weight scales (128 rows
+// x all of K: 8 KB up, 21 KB down), epilogue staging, barriers. The down half's larger slabs leave room for
+// four stages, the up half has five.
+template <int PH>
+struct BsPlan {
+    static constexpr int STAGES = PH == PH_UP ? 5 : 4;
+    static constexpr int SLAB = BM * (PH == PH_UP ? G_UP : G_DN);
+    static constexpr int OFF_SLAB = STAGES * BS_STAGE;
+    static constexpr int OFF_STG = OFF_SLAB + 2 * SLAB;
+    static constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;
+    static constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;
+    static constexpr int OFF_BAR = OFF_RED + 32;
+    static constexpr int NBAR = 2 * STAGES + 6;
+    static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+    static constexpr int OFF_ABORT = OFF_TMEM + 16;
+    static constexpr int SMEM = OFF_ABORT + 16 + 1024;
+    static_assert(SMEM <= 232448, "fits the 227 KB opt-in");
+    static_assert(SLAB % 16 == 0, "bulk copy size");
+};
+constexpr int BS_NA = 2, BS_NB = 2;                   // A issuers, B issuers
+constexpr int BS_W_A = 4, BS_W_B = BS_W_A + BS_NA, BS_W_SF = BS_W_B + BS_NB, BS_W_MMA = BS_W_SF + 1;
 constexpr int BS_THREADS = (BS_W_MMA + 1) * 32;
 constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and NT; scale factors from 2*NT
 constexpr int BS_SF_COL = 2 * NT;
@@ -839,11 +859,22 @@ __device__ __forceinline__ void nvfp4_planes16(float (&v)[16], uint32_t (&codes)
     }
 }
 
+// Scale byte offset of a pair inside its tile's atoms: row j of the tile -> (j % 32) * 16 + (j / 32) * 4.
+__device__ __forceinline__ int64_t sfb_row_offset(const Params &p, int pr, int ks_per_row, int &tile) {
+    tile = p.pair_tile[pr];
+    const int j = pr - p.tiles[tile].y;
+    return (int64_t)tile * ks_per_row * NP * BS_ATOM + (j & 31) * 16 + (j >> 5) * 4;
+}
+
 // One warp per sorted pair: x[token] * 2^E (amax in [2^8, 2^9)) as NP planes; E per pair for the epilogue.
+// The codes go to xq (row-major per plane); the scales straight into the tile's atoms (sfbx), so that the
+// GEMM moves a stage's scales with one bulk copy.
 __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (pr >= p.eoff[p.ne]) return;
+    int tile;
+    uint8_t *sfb = p.sfbx + sfb_row_offset(p, pr, KS_UP, tile);
     const int t = p.pair_tok[pr];
     float v[32];
     if (p.x_dtype == QMOE_DT_BF16) {
@@ -870,8 +901,9 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const int E = prescale_exp(amax, 9);
     const float scl = pow2f(E);
+    uint32_t sc2[NP] = {};   // this lane's two scale bytes per plane (groups 2*lane, 2*lane+1)
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {   // groups 2*lane, 2*lane+1 of the row
+    for (int g = 0; g < 2; ++g) {
         float w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) w[i] = v[16 * g + i] * scl;
@@ -882,8 +914,14 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
 #pragma unroll
         for (int pl = 0; pl < NP; ++pl) {
             *reinterpret_cast<uint2 *>(p.xq + ((int64_t)pl * p.P + pr) * (LAT / 2) + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
-            p.xsc[((int64_t)pl * p.P + pr) * G_UP + grp] = sc[pl];
+            sc2[pl] |= (uint32_t)sc[pl] << (8 * g);
         }
+    }
+    // k-step ks = lane / 2 holds groups 4ks .. 4ks+3: the even lane stores all four bytes
+#pragma unroll
+    for (int pl = 0; pl < NP; ++pl) {
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, sc2[pl], 1);
+        if (!(lane & 1)) *reinterpret_cast<uint32_t *>(sfb + ((lane >> 1) * NP + pl) * BS_ATOM) = sc2[pl] | (hi << 16);
     }
     if (lane == 0) p.pair_exp[pr] = E;
 }
@@ -895,35 +933,44 @@ __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (pr >= p.eoff[p.ne]) return;
-    const int tile = p.pair_tile[pr];
+    int tile;
+    uint8_t *sfb = p.sfbh + sfb_row_offset(p, pr, KS_DN, tile);
     const int sb_l = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
     int s0 = sb_l;
 #pragma unroll
     for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
-    for (int g0 = 0; g0 < G_DN; g0 += 32) {
+    for (int g0 = 0; g0 < G_DN; g0 += 32) {   // G_DN = 168 = 4 * 42: lanes of one k-step are all in or all out
         const int grp = g0 + lane;
-        const int blkid = (grp < G_DN ? grp : G_DN - 1) >> 3;
+        const bool live = grp < G_DN;
+        const int blkid = (live ? grp : G_DN - 1) >> 3;
         const int sbk = __shfl_sync(0xffffffffu, sb_l, blkid);
-        if (grp >= G_DN) continue;
-        const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
-        const float f = d >= -126 ? pow2f(d) : 0.f;
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
-        const uint4 a = src[0], b = src[1];
-        const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        float w[16];
+        uint8_t sc[NP] = {};
+        if (live) {
+            const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
+            const float f = d >= -126 ? pow2f(d) : 0.f;
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
+            const uint4 a = src[0], b = src[1];
+            const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            float w[16];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float2 q = __half22float2(as_h2(u[i]));
-            w[2 * i] = q.x * f;
-            w[2 * i + 1] = q.y * f;
+            for (int i = 0; i < 8; ++i) {
+                const float2 q = __half22float2(as_h2(u[i]));
+                w[2 * i] = q.x * f;
+                w[2 * i + 1] = q.y * f;
+            }
+            uint32_t codes[NP][2];
+            nvfp4_planes16(w, codes, sc);
+#pragma unroll
+            for (int pl = 0; pl < NP; ++pl)
+                *reinterpret_cast<uint2 *>(p.hq + ((int64_t)pl * p.P + pr) * KB_DN + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
         }
-        uint32_t codes[NP][2];
-        uint8_t sc[NP];
-        nvfp4_planes16(w, codes, sc);
+        // the four groups of k-step grp / 4 sit in lanes 4i .. 4i+3: gather their scale bytes in lane 4i
 #pragma unroll
         for (int pl = 0; pl < NP; ++pl) {
-            *reinterpret_cast<uint2 *>(p.hq + ((int64_t)pl * p.P + pr) * KB_DN + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
-            p.hsc[((int64_t)pl * p.P + pr) * G_DN + grp] = sc[pl];
+            uint32_t v = sc[pl];
+            v |= __shfl_down_sync(0xffffffffu, v, 1) << 8;
+            v |= __shfl_down_sync(0xffffffffu, v, 2) << 16;
+            if (live && !(lane & 3)) *reinterpret_cast<uint32_t *>(sfb + ((grp >> 2) * NP + pl) * BS_ATOM) = v;
         }
     }
 }
@@ -951,10 +998,11 @@ __device__ __forceinline__ uint32_t instr_desc_nvfp4(int n) {
 }
 
 // The grouped GEMM on block-scaled NVFP4 MMA; persistent, items (tile, 128 weight rows) as pf_gemm_kernel.
-// Roles: warps 4..5 load the weight stages (TMA, 8 KB, 64-byte swizzle), warps 6..7 the NP activation planes
-// of the stage (one 3-D TMA box: planes x pair rows x 64 B), warps 8..9 assemble the scale-factor atoms with
-// 4-byte cp.async; warp 10 copies the atoms into TMEM and issues NP MMAs per k-step; warps 0..3 drain the
-// other accumulator (epilogue as pf_gemm_kernel).
+// Roles: warps 4..5 load the weight stages (TMA, 8 KB, 64-byte swizzle); warps 6..7 the NP activation planes
+// of the stage (one 3-D TMA box: planes x pair rows x 64 B) and the planes' scale atoms (one 3 KB bulk copy,
+// laid out by the plane kernels); warp 8 bulk-copies the item's 128 weight-scale rows into a slab and
+// rearranges each stage's two weight atoms from it; warp 9 copies the atoms into TMEM and issues NP MMAs per
+// k-step; warps 0..3 drain the other accumulator (epilogue as pf_gemm_kernel).
 template <int PH>
 __global__ void __launch_bounds__(BS_THREADS, 1)
     pfb_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b16,
@@ -963,32 +1011,37 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     constexpr int MT = PH == PH_UP ? MT_UP : MT_DN;
     constexpr int K = PH == PH_UP ? LAT : INTER;
     constexpr int NST = K / BS_BK;                     // stages per item
-    constexpr int GP = PH == PH_UP ? G_UP : G_DN;      // scale bytes per row (weights and planes)
+    constexpr int GP = PH == PH_UP ? G_UP : G_DN;      // scale bytes per weight row
+    constexpr int KS = K / 64;                         // MMA k-steps per row
+    using Plan = BsPlan<PH>;
+    constexpr int S = Plan::STAGES;
     const int nitems = *p.tile_count * MT;
 
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw_base = smem_u32(smem_raw);
     uint8_t *sm = smem_raw + (((raw_base + 1023u) & ~1023u) - raw_base);
     const uint32_t sbase = smem_u32(sm);
-    float *colsc = reinterpret_cast<float *>(sm + BS_OFF_COLSC);
-    float *red = reinterpret_cast<float *>(sm + BS_OFF_RED);
-    __half *stg = reinterpret_cast<__half *>(sm + BS_OFF_STG);
-    uint64_t *full = reinterpret_cast<uint64_t *>(sm + BS_OFF_BAR);
-    uint64_t *empty = full + BS_STAGES;
-    uint64_t *acc_full = empty + BS_STAGES;
+    float *colsc = reinterpret_cast<float *>(sm + Plan::OFF_COLSC);
+    float *red = reinterpret_cast<float *>(sm + Plan::OFF_RED);
+    __half *stg = reinterpret_cast<__half *>(sm + Plan::OFF_STG);
+    uint64_t *full = reinterpret_cast<uint64_t *>(sm + Plan::OFF_BAR);
+    uint64_t *empty = full + S;
+    uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + BS_OFF_TMEM);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + BS_OFF_ABORT);
+    uint64_t *slab_full = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int s = 0; s < BS_STAGES; s++) {
-            mbar_init(&full[s], 2 + BS_NSF * 32);   // A and B expect_tx arrivals + one per scale loader thread
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 3);   // A and B expect_tx arrivals, the weight-atom warp
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&acc_full[a], 1);
             mbar_init(&acc_empty[a], 4);
+            mbar_init(&slab_full[a], 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -1016,8 +1069,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 bool ok = true;
                 for (int kt = 0; kt < NST; kt++, q++) {
                     if ((int)(q % BS_NA) != pr) continue;
-                    const int s = q % BS_STAGES;
-                    if (!lane_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, abort_flag, p.status)) {
+                    const int s = q % S;
+                    if (!lane_wait(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -1031,8 +1084,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         __syncwarp();
     } else if (warp >= BS_W_B && warp < BS_W_SF) {
         // ------------------------------------------------------------ activation planes [NP][rows][64 B] per stage
+        //                                                              and their scale atoms [k-step][plane][512 B]
         const int pb = warp - BS_W_B;
         if (lane == 0) {
+            const uint8_t *sfb = PH == PH_UP ? p.sfbx : p.sfbh;
             uint32_t q = 0;
             int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
             for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
@@ -1040,64 +1095,85 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
                 const int n0 = td.y, np_ = b_rows(td.z);
                 const CUtensorMap *map = np_ == 16 ? &tm_b16 : np_ == 32 ? &tm_b32 : np_ == 64 ? &tm_b64 : &tm_b128;
+                const uint8_t *sfb_tile = sfb + (int64_t)(i / MT) * KS * NP * BS_ATOM;
                 bool ok = true;
                 for (int kt = 0; kt < NST; kt++, q++) {
                     if ((int)(q % BS_NB) != pb) continue;
-                    const int s = q % BS_STAGES;
-                    if (!lane_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, abort_flag, p.status)) {
+                    const int s = q % S;
+                    if (!lane_wait(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2)));
+                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2) + BS_SFB));
                     tma_load_3d(sm + s * BS_STAGE + BS_A, map, kt * (BS_BK / 2), n0, 0, &full[s]);
+                    bulk_g2s_nohint(sm + s * BS_STAGE + BS_A + BS_B, sfb_tile + (int64_t)kt * BS_SFB, BS_SFB, &full[s]);
                 }
                 if (!ok) break;
             }
         }
         __syncwarp();
-    } else if (warp >= BS_W_SF && warp < BS_W_MMA) {
-        // ------------------------------------------------------------ scale-factor atoms by 4-byte cp.async
-        const int st = tid - BS_W_SF * 32;   // 0 .. 63
-        const uint8_t *psc = PH == PH_UP ? p.xsc : p.hsc;
+    } else if (warp == BS_W_SF) {
+        // ------------------------------------------------------------ weight-scale atoms
+        // The item's scale rows (128 rows x GP bytes, contiguous in the block) arrive by one bulk copy into one
+        // of two slabs, the next item's copy in flight while this item is built. Stage kt takes bytes
+        // 8kt .. 8kt+7 of each row: atom kk, lane L = rows L, L+32, L+64, L+96, 4 bytes each.
+        uint8_t *slab = sm + Plan::OFF_SLAB;
+        const uint8_t *wsc0 = p.store + (PH == PH_UP ? O_US : O_DS);
+        uint32_t issued[2] = {0, 0}, done[2] = {0, 0};
+        if (blockIdx.x < nitems) {
+            if (lane == 0) {
+                const int i = blockIdx.x;
+                mbar_expect_tx(&slab_full[0], Plan::SLAB);
+                bulk_g2s_nohint(slab, wsc0 + (int64_t)p.tiles[i / MT].x * p.bstride + (int64_t)(i % MT) * Plan::SLAB,
+                                Plan::SLAB, &slab_full[0]);
+            }
+            issued[0] = 1;
+        }
         uint32_t q = 0;
-        int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
-        for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
-            const int4 td = td_next;
-            if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
-            const int e = td.x, n0 = td.y, n = td.z, mt = i % MT;
-            const uint8_t *wsc = p.store + (int64_t)e * p.bstride + (PH == PH_UP ? O_US : O_DS) + (int64_t)mt * BM * GP;
+        for (int i = blockIdx.x, j = 0; i < nitems; i += gridDim.x, j++) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;   // one decision for the whole warp
+            const int b = j & 1;
+            const int inext = i + (int)gridDim.x;
+            if (inext < nitems) {   // slab b ^ 1 was last read while building item j - 1
+                __syncwarp();
+                if (lane == 0) {
+                    fence_async_smem();
+                    mbar_expect_tx(&slab_full[b ^ 1], Plan::SLAB);
+                    bulk_g2s_nohint(slab + (b ^ 1) * Plan::SLAB,
+                                    wsc0 + (int64_t)p.tiles[inext / MT].x * p.bstride + (int64_t)(inext % MT) * Plan::SLAB,
+                                    Plan::SLAB, &slab_full[b ^ 1]);
+                }
+                issued[b ^ 1]++;
+            }
+            if (!warp_wait(&slab_full[b], (j >> 1) & 1, lane, abort_flag, p.status)) break;
+            mbar_try_wait(&slab_full[b], (j >> 1) & 1);   // completed phase: acquire for every lane
+            done[b]++;
+            const uint8_t *sl = slab + b * Plan::SLAB;
             bool ok = true;
             for (int kt = 0; kt < NST; kt++, q++) {
-                const int s = q % BS_STAGES;
-                if (!warp_wait(&empty[s], ((q / BS_STAGES) & 1) ^ 1, lane, abort_flag, p.status)) {
+                const int s = q % S;
+                if (!warp_wait(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
-                const uint32_t sf = sbase + s * BS_STAGE + BS_A + BS_B;
-                const int per = BM + NP * n;   // rows of one k-step: weight rows, then the planes' pair rows
-                for (int w = st; w < BS_KS * per; w += BS_NSF * 32) {
-                    const int kk = w / per, rr = w - kk * per;
-                    const int ks = kt * BS_KS + kk;   // k-step: scale bytes 4ks .. 4ks+3 of the row
-                    const uint8_t *src;
-                    int row, atom;
-                    if (rr < BM) {
-                        row = rr;
-                        atom = kk * (1 + NP);
-                        src = wsc + (int64_t)row * GP + 4 * ks;
-                    } else {
-                        const int pl = (rr - BM) / n;
-                        row = (rr - BM) - pl * n;
-                        atom = kk * (1 + NP) + 1 + pl;
-                        src = psc + ((int64_t)pl * p.P + n0 + row) * GP + 4 * ks;
-                    }
-                    const uint32_t dst = sf + atom * BS_ATOM + (row & 31) * 16 + (row >> 5) * 4;
-                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
-                }
-                asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&full[s])) : "memory");
+                uint2 w[4];
+#pragma unroll
+                for (int g = 0; g < 4; g++) w[g] = *reinterpret_cast<const uint2 *>(sl + (lane + 32 * g) * GP + 8 * kt);
+                uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B + BS_SFB;
+                *reinterpret_cast<uint4 *>(at + lane * 16) = make_uint4(w[0].x, w[1].x, w[2].x, w[3].x);
+                *reinterpret_cast<uint4 *>(at + BS_ATOM + lane * 16) = make_uint4(w[0].y, w[1].y, w[2].y, w[3].y);
+                fence_async_smem();   // generic-proxy atom stores -> visible to tcgen05.cp
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[s]);
             }
             if (!ok) break;
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        // after an abort: let every slab copy still in flight land before the CTA exits (bounded waits)
+        if (lane == 0)
+            for (int b = 0; b < 2; b++)
+                for (; done[b] < issued[b]; done[b]++)
+                    if (!mbar_wait(&slab_full[b], done[b] & 1)) break;
+        __syncwarp();
     } else if (warp == BS_W_MMA) {
         // ------------------------------------------------------------ scale factors -> TMEM, NP MMAs per k-step
         if (lane == 0) {
@@ -1114,21 +1190,20 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const uint32_t d = tmem + a * NT;
                 bool ok = true;
                 for (int kt = 0; kt < NST; kt++, q++) {
-                    const int s = q % BS_STAGES;
-                    if (!lane_wait(&full[s], (q / BS_STAGES) & 1, abort_flag, p.status)) {
+                    const int s = q % S;
+                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
-                    fence_async_smem();   // the cp.async-written scale atoms -> visible to the async proxy
                     tc_fence_after();
                     const uint32_t st0 = sbase + s * BS_STAGE;
 #pragma unroll
                     for (int kk = 0; kk < BS_KS; kk++) {
                         const uint32_t sfa = tmem + BS_SF_COL + kk * 16;   // 4 columns SFA, then 4 per plane
-                        const uint32_t atoms = st0 + BS_A + BS_B + kk * (1 + NP) * BS_ATOM;
-                        tmem_cp_sf(sfa, atoms);
+                        const uint32_t atoms_b = st0 + BS_A + BS_B + kk * NP * BS_ATOM;
+                        tmem_cp_sf(sfa, st0 + BS_A + BS_B + BS_SFB + kk * BS_ATOM);
 #pragma unroll
-                        for (int pl = 0; pl < NP; pl++) tmem_cp_sf(sfa + 4 + 4 * pl, atoms + (1 + pl) * BS_ATOM);
+                        for (int pl = 0; pl < NP; pl++) tmem_cp_sf(sfa + 4 + 4 * pl, atoms_b + pl * BS_ATOM);
                         const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
 #pragma unroll
                         for (int pl = 0; pl < NP; pl++) {
@@ -1233,7 +1308,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
     size_t status, tile_count, cnt, eoff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
-        hs, op, pair_tile, xq, xsc, hq, hsc, total;
+        hs, op, pair_tile, xq, hq, sfbx, sfbh, total;
     int P, nchunks, tiles_cap;
 };
 
@@ -1265,9 +1340,9 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.op = take((size_t)L.P * LAT * 4);
     L.pair_tile = take(sizeof(int) * (size_t)L.P);
     L.xq = take((size_t)NP * L.P * (LAT / 2));
-    L.xsc = take((size_t)NP * L.P * G_UP);
     L.hq = take((size_t)NP * L.P * KB_DN);
-    L.hsc = take((size_t)NP * L.P * G_DN);
+    L.sfbx = take((size_t)L.tiles_cap * KS_UP * NP * BS_ATOM);
+    L.sfbh = take((size_t)L.tiles_cap * KS_DN * NP * BS_ATOM);
     L.total = o;
     return L;
 }
@@ -1394,9 +1469,9 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.op = reinterpret_cast<float *>(ws + L.op);
     p.pair_tile = reinterpret_cast<int *>(ws + L.pair_tile);
     p.xq = ws + L.xq;
-    p.xsc = ws + L.xsc;
     p.hq = ws + L.hq;
-    p.hsc = ws + L.hsc;
+    p.sfbx = ws + L.sfbx;
+    p.sfbh = ws + L.sfbh;
 
     // up: block-scaled NVFP4 (weights as stored, x as NVFP4 planes); down: block-scaled on the orig layout,
     // or the exact-f16 kernel on the T layout (FP4 operands of the tensor core must be K-major)
@@ -1417,9 +1492,9 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
         return QMOE_ERR_LAUNCH;
     }
     auto up = pfb_gemm_kernel<PH_UP>;
-    if (!ensure_smem(up, BS_SMEM, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
+    if (!ensure_smem(up, BsPlan<PH_UP>::SMEM, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
     if (layout_T ? !ensure_smem(pf_gemm_kernel<PH_DN_T>, SMEM_BYTES, dev, g_smem_dn_t)
-                 : !ensure_smem(pfb_gemm_kernel<PH_DN_O>, BS_SMEM, dev, g_smem_dn_o))
+                 : !ensure_smem(pfb_gemm_kernel<PH_DN_O>, BsPlan<PH_DN_O>::SMEM, dev, g_smem_dn_o))
         return QMOE_ERR_LAUNCH;
 
     cudaStream_t st = as_stream(stream);
@@ -1427,12 +1502,12 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
     pf_xplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-    up<<<di->sms, BS_THREADS, BS_SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
+    up<<<di->sms, BS_THREADS, BsPlan<PH_UP>::SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
     if (layout_T) {
         pf_gemm_kernel<PH_DN_T><<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wdt, wdt, sdt);
     } else {
         pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-        pfb_gemm_kernel<PH_DN_O><<<di->sms, BS_THREADS, BS_SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
+        pfb_gemm_kernel<PH_DN_O><<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
     }
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
