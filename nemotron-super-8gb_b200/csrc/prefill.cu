@@ -811,7 +811,7 @@ struct BsPlan {
     static constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;
     static constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;
     static constexpr int OFF_BAR = OFF_RED + 32;
-    static constexpr int NBAR = 2 * STAGES + 6;
+    static constexpr int NBAR = 3 * STAGES + 8;
     static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
     static constexpr int OFF_ABORT = OFF_TMEM + 16;
     static constexpr int SMEM = OFF_ABORT + 16 + 1024;
@@ -820,9 +820,12 @@ struct BsPlan {
 };
 constexpr int BS_NA = 2, BS_NB = 2;                   // A issuers, B issuers
 constexpr int BS_W_A = 4, BS_W_B = BS_W_A + BS_NA, BS_W_SF = BS_W_B + BS_NB, BS_W_MMA = BS_W_SF + 1;
-constexpr int BS_THREADS = (BS_W_MMA + 1) * 32;
-constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and NT; scale factors from 2*NT
-constexpr int BS_SF_COL = 2 * NT;
+constexpr int BS_NCP = 2;                             // scale-copy warps: warp c copies k-step c of a stage
+constexpr int BS_W_CP = BS_W_MMA + 1;
+constexpr int BS_THREADS = (BS_W_CP + BS_NCP) * 32;
+constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and NT; stage s's scale factors at
+constexpr int BS_SF_COL = 2 * NT;                     // 2*NT + 32 s (per k-step: 4 columns SFA, 4 per plane)
+static_assert(BS_SF_COL + 32 * 5 <= BS_TMEM_COLS && BS_KS * (1 + NP) * 4 <= 32, "TMEM plan");
 
 // Pair rows loaded for a tile of n pairs (the TMA box heights).
 __device__ __forceinline__ int b_rows(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
@@ -1029,6 +1032,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *slab_full = acc_empty + 2;
+    uint64_t *sf_full = slab_full + 2;   // [S] the stage's scale factors are in TMEM (both copy warps)
+    uint64_t *cp_done = sf_full + S;     // [2] end of each copy warp
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
 
@@ -1042,7 +1047,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             mbar_init(&acc_full[a], 1);
             mbar_init(&acc_empty[a], 4);
             mbar_init(&slab_full[a], 1);
+            mbar_init(&cp_done[a], 1);
         }
+        for (int s = 0; s < S; s++) mbar_init(&sf_full[s], BS_NCP);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -1191,7 +1198,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 bool ok = true;
                 for (int kt = 0; kt < NST; kt++, q++) {
                     const int s = q % S;
-                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status)) {
+                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status) ||
+                        !lane_wait(&sf_full[s], (q / S) & 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -1199,11 +1207,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     const uint32_t st0 = sbase + s * BS_STAGE;
 #pragma unroll
                     for (int kk = 0; kk < BS_KS; kk++) {
-                        const uint32_t sfa = tmem + BS_SF_COL + kk * 16;   // 4 columns SFA, then 4 per plane
-                        const uint32_t atoms_b = st0 + BS_A + BS_B + kk * NP * BS_ATOM;
-                        tmem_cp_sf(sfa, st0 + BS_A + BS_B + BS_SFB + kk * BS_ATOM);
-#pragma unroll
-                        for (int pl = 0; pl < NP; pl++) tmem_cp_sf(sfa + 4 + 4 * pl, atoms_b + pl * BS_ATOM);
+                        const uint32_t sfa = tmem + BS_SF_COL + s * 32 + kk * 16;
                         const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
 #pragma unroll
                         for (int pl = 0; pl < NP; pl++) {
@@ -1216,6 +1220,38 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 mma_commit(&acc_full[a]);   // also after a failed wait: tracks every MMA issued
                 if (!ok) break;
             }
+        }
+        __syncwarp();
+    } else if (warp >= BS_W_CP) {
+        // ------------------------------------------------------------ scale-factor atoms -> TMEM slot of the stage
+        // Copies run on their own issuing threads, beside the MMAs. Slot s is rewritten only after full[s] of
+        // its next use, which follows empty[s] (the MMAs that read the slot completed) through the producers.
+        const int c = warp - BS_W_CP;
+        if (lane == 0) {
+            uint32_t q = 0;
+            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
+                bool ok = true;
+                for (int kt = 0; kt < NST; kt++, q++) {
+                    const int s = q % S;
+                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t st0 = sbase + s * BS_STAGE;
+                    for (int kk = c; kk < BS_KS; kk += BS_NCP) {
+                        const uint32_t sfa = tmem + BS_SF_COL + s * 32 + kk * 16;
+                        tmem_cp_sf(sfa, st0 + BS_A + BS_B + BS_SFB + kk * BS_ATOM);
+#pragma unroll
+                        for (int pl = 0; pl < NP; pl++)
+                            tmem_cp_sf(sfa + 4 + 4 * pl, st0 + BS_A + BS_B + (kk * NP + pl) * BS_ATOM);
+                    }
+                    mma_commit(&sf_full[s]);
+                }
+                if (!ok) break;
+            }
+            mma_commit(&cp_done[c]);
+            mbar_wait(&cp_done[c], 0);   // this warp's copies have landed before TMEM is released (bounded)
         }
         __syncwarp();
     } else {
