@@ -348,6 +348,16 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
 }
 
 // 32 lanes x 16 consecutive f32 columns of tensor memory -> 16 registers per thread.
+// 16 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers (thread i -> lane base + i).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
@@ -820,9 +830,9 @@ struct BsPlan {
 };
 constexpr int BS_NA = 2, BS_NB = 2;                   // A issuers, B issuers
 constexpr int BS_W_A = 4, BS_W_B = BS_W_A + BS_NA, BS_W_SF = BS_W_B + BS_NB, BS_W_MMA = BS_W_SF + 1;
-constexpr int BS_NCP = 2;                             // scale-copy warps: warp c copies k-step c of a stage
-constexpr int BS_W_CP = BS_W_MMA + 1;
-constexpr int BS_THREADS = (BS_W_CP + BS_NCP) * 32;
+constexpr int BS_NSS = 4;                             // scale-store warps: one per TMEM lane quarter
+constexpr int BS_W_SS = BS_W_MMA + 1;
+constexpr int BS_THREADS = (BS_W_SS + BS_NSS) * 32;
 constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and NT; stage s's scale factors at
 constexpr int BS_SF_COL = 2 * NT;                     // 2*NT + 32 s (per k-step: 4 columns SFA, 4 per plane)
 static_assert(BS_SF_COL + 32 * 5 <= BS_TMEM_COLS && BS_KS * (1 + NP) * 4 <= 32, "TMEM plan");
@@ -862,11 +872,17 @@ __device__ __forceinline__ void nvfp4_planes16(float (&v)[16], uint32_t (&codes)
     }
 }
 
-// Scale byte offset of a pair inside its tile's atoms: row j of the tile -> (j % 32) * 16 + (j / 32) * 4.
-__device__ __forceinline__ int64_t sfb_row_offset(const Params &p, int pr, int ks_per_row, int &tile) {
-    tile = p.pair_tile[pr];
-    const int j = pr - p.tiles[tile].y;
-    return (int64_t)tile * ks_per_row * NP * BS_ATOM + (j & 31) * 16 + (j >> 5) * 4;
+// A tile of h = b_rows(n) <= 32 pair rows runs its NP planes as ONE MMA of N = NP * h: B row pl * h + j is
+// pair j of plane pl (the planes lie contiguous in the stage), and its scales sit in the tile's plane-0 atom
+// at that row. Larger tiles run one MMA per plane with plane pl's scales in atom pl at row j.
+__device__ __forceinline__ bool fused_planes(int h) { return h <= 32; }
+
+// Byte of the tile's atoms holding the 4 scales of k-step ks, plane pl, pair j (atom row r:
+// (r % 32) * 16 + (r / 32) * 4).
+__device__ __forceinline__ int sfb_byte(int ks, int pl, int j, int h) {
+    const bool f = fused_planes(h);
+    const int r = f ? pl * h + j : j;
+    return (ks * NP + (f ? 0 : pl)) * BS_ATOM + (r & 31) * 16 + (r >> 5) * 4;
 }
 
 // One warp per sorted pair: x[token] * 2^E (amax in [2^8, 2^9)) as NP planes; E per pair for the epilogue.
@@ -876,8 +892,10 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (pr >= p.eoff[p.ne]) return;
-    int tile;
-    uint8_t *sfb = p.sfbx + sfb_row_offset(p, pr, KS_UP, tile);
+    const int tile = p.pair_tile[pr];
+    const int4 td = p.tiles[tile];
+    const int jrow = pr - td.y, h = b_rows(td.z);
+    uint8_t *sfb = p.sfbx + (int64_t)tile * KS_UP * NP * BS_ATOM;
     const int t = p.pair_tok[pr];
     float v[32];
     if (p.x_dtype == QMOE_DT_BF16) {
@@ -924,7 +942,7 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
 #pragma unroll
     for (int pl = 0; pl < NP; ++pl) {
         const uint32_t hi = __shfl_down_sync(0xffffffffu, sc2[pl], 1);
-        if (!(lane & 1)) *reinterpret_cast<uint32_t *>(sfb + ((lane >> 1) * NP + pl) * BS_ATOM) = sc2[pl] | (hi << 16);
+        if (!(lane & 1)) *reinterpret_cast<uint32_t *>(sfb + sfb_byte(lane >> 1, pl, jrow, h)) = sc2[pl] | (hi << 16);
     }
     if (lane == 0) p.pair_exp[pr] = E;
 }
@@ -936,8 +954,10 @@ __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (pr >= p.eoff[p.ne]) return;
-    int tile;
-    uint8_t *sfb = p.sfbh + sfb_row_offset(p, pr, KS_DN, tile);
+    const int tile = p.pair_tile[pr];
+    const int4 td = p.tiles[tile];
+    const int jrow = pr - td.y, h = b_rows(td.z);
+    uint8_t *sfb = p.sfbh + (int64_t)tile * KS_DN * NP * BS_ATOM;
     const int sb_l = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
     int s0 = sb_l;
 #pragma unroll
@@ -973,7 +993,7 @@ __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
             uint32_t v = sc[pl];
             v |= __shfl_down_sync(0xffffffffu, v, 1) << 8;
             v |= __shfl_down_sync(0xffffffffu, v, 2) << 16;
-            if (live && !(lane & 3)) *reinterpret_cast<uint32_t *>(sfb + ((grp >> 2) * NP + pl) * BS_ATOM) = v;
+            if (live && !(lane & 3)) *reinterpret_cast<uint32_t *>(sfb + sfb_byte(grp >> 2, pl, jrow, h)) = v;
         }
     }
 }
@@ -1004,8 +1024,36 @@ __device__ __forceinline__ uint32_t instr_desc_nvfp4(int n) {
 // Roles: warps 4..5 load the weight stages (TMA, 8 KB, 64-byte swizzle); warps 6..7 the NP activation planes
 // of the stage (one 3-D TMA box: planes x pair rows x 64 B) and the planes' scale atoms (one 3 KB bulk copy,
 // laid out by the plane kernels); warp 8 bulk-copies the item's 128 weight-scale rows into a slab and
-// rearranges each stage's two weight atoms from it; warp 9 copies the atoms into TMEM and issues NP MMAs per
-// k-step; warps 0..3 drain the other accumulator (epilogue as pf_gemm_kernel).
+// rearranges each stage's two weight atoms from it; warps 10..13 store the stage's atoms into its TMEM scale
+// slot; warp 9 issues NP MMAs per k-step; warps 0..3 drain the other accumulator (epilogue as pf_gemm_kernel).
+// Waits of the producer and epilogue roles: between polls the thread sleeps, so that polling warps leave the
+// issue slots of their SM sub-partition to the MMA-issuing warp.
+__device__ __forceinline__ bool mbar_wait_bo(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(200);
+        if (clock64() - t0 > WAIT_CYCLES) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool lane_wait_bo(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+    const bool ok = !*abort_flag && mbar_wait_bo(bar, parity);
+    if (!ok) {
+        set_error(status, DEV_ERR_TIMEOUT);
+        *abort_flag = 1;
+    }
+    return ok;
+}
+
+__device__ __forceinline__ bool warp_wait_bo(uint64_t *bar, uint32_t parity, int lane, volatile int *abort_flag,
+                                             int *status) {
+    bool ok = true;
+    if (lane == 0) ok = lane_wait_bo(bar, parity, abort_flag, status);
+    return __shfl_sync(0xffffffffu, ok, 0);
+}
+
 template <int PH>
 __global__ void __launch_bounds__(BS_THREADS, 1)
     pfb_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b16,
@@ -1032,8 +1080,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *slab_full = acc_empty + 2;
-    uint64_t *sf_full = slab_full + 2;   // [S] the stage's scale factors are in TMEM (both copy warps)
-    uint64_t *cp_done = sf_full + S;     // [2] end of each copy warp
+    uint64_t *sf_full = slab_full + 2;   // [S] the stage's scale factors are in TMEM (all four store warps)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
 
@@ -1047,9 +1094,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             mbar_init(&acc_full[a], 1);
             mbar_init(&acc_empty[a], 4);
             mbar_init(&slab_full[a], 1);
-            mbar_init(&cp_done[a], 1);
         }
-        for (int s = 0; s < S; s++) mbar_init(&sf_full[s], BS_NCP);
+        for (int s = 0; s < S; s++) mbar_init(&sf_full[s], BS_NSS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -1077,7 +1123,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 for (int kt = 0; kt < NST; kt++, q++) {
                     if ((int)(q % BS_NA) != pr) continue;
                     const int s = q % S;
-                    if (!lane_wait(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
+                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -1107,7 +1153,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 for (int kt = 0; kt < NST; kt++, q++) {
                     if ((int)(q % BS_NB) != pb) continue;
                     const int s = q % S;
-                    if (!lane_wait(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
+                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -1152,14 +1198,14 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 }
                 issued[b ^ 1]++;
             }
-            if (!warp_wait(&slab_full[b], (j >> 1) & 1, lane, abort_flag, p.status)) break;
+            if (!warp_wait_bo(&slab_full[b], (j >> 1) & 1, lane, abort_flag, p.status)) break;
             mbar_try_wait(&slab_full[b], (j >> 1) & 1);   // completed phase: acquire for every lane
             done[b]++;
             const uint8_t *sl = slab + b * Plan::SLAB;
             bool ok = true;
             for (int kt = 0; kt < NST; kt++, q++) {
                 const int s = q % S;
-                if (!warp_wait(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status)) {
+                if (!warp_wait_bo(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
@@ -1190,10 +1236,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const int n = n_next;
                 if (i + (int)gridDim.x < nitems) n_next = p.tiles[(i + gridDim.x) / MT].z;
                 const int np_ = b_rows(n);
+                const bool fused = fused_planes(np_);
                 const int a = j & 1;
                 if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
                 tc_fence_after();
-                const uint32_t idesc = instr_desc_nvfp4((n + 15) & ~15);
+                const uint32_t idesc = instr_desc_nvfp4(fused ? NP * np_ : (n + 15) & ~15);
                 const uint32_t d = tmem + a * NT;
                 bool ok = true;
                 for (int kt = 0; kt < NST; kt++, q++) {
@@ -1209,10 +1256,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     for (int kk = 0; kk < BS_KS; kk++) {
                         const uint32_t sfa = tmem + BS_SF_COL + s * 32 + kk * 16;
                         const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
+                        if (fused) {   // all planes: N = NP * np_ rows of B, scales in the plane-0 atom
+                            const uint64_t bd = smem_desc(st0 + BS_A + kk * 32, 16, 512, 4);
+                            mma_nvfp4(d, ad, bd, idesc, (kt | kk) != 0, sfa, sfa + 4);
+                        } else {
 #pragma unroll
-                        for (int pl = 0; pl < NP; pl++) {
-                            const uint64_t bd = smem_desc(st0 + BS_A + pl * np_ * (BS_BK / 2) + kk * 32, 16, 512, 4);
-                            mma_nvfp4(d, ad, bd, idesc, (kt | kk | pl) != 0, sfa, sfa + 4 + 4 * pl);
+                            for (int pl = 0; pl < NP; pl++) {
+                                const uint64_t bd = smem_desc(st0 + BS_A + pl * np_ * (BS_BK / 2) + kk * 32, 16, 512, 4);
+                                mma_nvfp4(d, ad, bd, idesc, (kt | kk | pl) != 0, sfa, sfa + 4 + 4 * pl);
+                            }
                         }
                     }
                     mma_commit(&empty[s]);
@@ -1222,38 +1274,44 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             }
         }
         __syncwarp();
-    } else if (warp >= BS_W_CP) {
+    } else if (warp >= BS_W_SS) {
         // ------------------------------------------------------------ scale-factor atoms -> TMEM slot of the stage
-        // Copies run on their own issuing threads, beside the MMAs. Slot s is rewritten only after full[s] of
-        // its next use, which follows empty[s] (the MMAs that read the slot completed) through the producers.
-        const int c = warp - BS_W_CP;
-        if (lane == 0) {
-            uint32_t q = 0;
-            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
-                bool ok = true;
-                for (int kt = 0; kt < NST; kt++, q++) {
-                    const int s = q % S;
-                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t st0 = sbase + s * BS_STAGE;
-                    for (int kk = c; kk < BS_KS; kk += BS_NCP) {
-                        const uint32_t sfa = tmem + BS_SF_COL + s * 32 + kk * 16;
-                        tmem_cp_sf(sfa, st0 + BS_A + BS_B + BS_SFB + kk * BS_ATOM);
-#pragma unroll
-                        for (int pl = 0; pl < NP; pl++)
-                            tmem_cp_sf(sfa + 4 + 4 * pl, st0 + BS_A + BS_B + (kk * NP + pl) * BS_ATOM);
-                    }
-                    mma_commit(&sf_full[s]);
+        // tcgen05.st from four warps, warp w writing lane quarter w % 4: each quarter gets the 32-row pattern of
+        // every atom (lane L, column c = bytes 16L + 4c .. 16L + 4c + 3), the layout a 32x128b.warpx4 copy
+        // makes, without occupying the tensor pipe. Slot s is rewritten only after full[s] of its next use,
+        // which follows empty[s] (the MMAs that read the slot completed) through the producers.
+        const uint32_t quarter = (uint32_t)(warp & 3) << 21;   // TMEM lane 32 * (warp % 4), in bits 16..
+        uint32_t q = 0;
+        for (int i = blockIdx.x; i < nitems; i += gridDim.x) {
+            if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;   // one decision for the whole warp
+            bool ok = true;
+            for (int kt = 0; kt < NST; kt++, q++) {
+                const int s = q % S;
+                if (!warp_wait_bo(&full[s], (q / S) & 1, lane, abort_flag, p.status)) {
+                    ok = false;
+                    break;
                 }
-                if (!ok) break;
+                mbar_try_wait(&full[s], (q / S) & 1);   // completed phase: acquire for every lane
+                const uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B;
+#pragma unroll
+                for (int kk = 0; kk < BS_KS; kk++) {
+                    uint32_t r[16];
+                    const uint4 a = *reinterpret_cast<const uint4 *>(at + BS_SFB + kk * BS_ATOM + lane * 16);
+                    r[0] = a.x, r[1] = a.y, r[2] = a.z, r[3] = a.w;
+#pragma unroll
+                    for (int pl = 0; pl < NP; pl++) {
+                        const uint4 b = *reinterpret_cast<const uint4 *>(at + (kk * NP + pl) * BS_ATOM + lane * 16);
+                        r[4 + 4 * pl] = b.x, r[5 + 4 * pl] = b.y, r[6 + 4 * pl] = b.z, r[7 + 4 * pl] = b.w;
+                    }
+                    tmem_st16(tmem + quarter + BS_SF_COL + s * 32 + kk * 16, r);
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sf_full[s]);
             }
-            mma_commit(&cp_done[c]);
-            mbar_wait(&cp_done[c], 0);   // this warp's copies have landed before TMEM is released (bounded)
+            if (!ok) break;
         }
-        __syncwarp();
     } else {
         // ------------------------------------------------------------ epilogue (warps 0..3 = TMEM lanes)
         const int m = tid;
@@ -1269,15 +1327,42 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 else cs[jj] = p.pair_coef[n0 + jj] * p.s2[(int64_t)e * 2 + 1] * pow2f(min(HSHIFT - s0, 127));
             }
             named_sync(1, 128);
-            const bool acc_ok = warp_wait(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
+            const bool acc_ok = warp_wait_bo(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
             tc_fence_after();
             const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
+            // a fused-plane tile holds plane pl of pair c in column pl * h + c: the pair's value is the sum
+            const int h = b_rows(n);
+            const bool fused = fused_planes(h);
+            auto acc32 = [&](int c0, float(&v)[32]) {
+                tmem_ld32(trow + c0, v);
+                if (fused) {
+#pragma unroll
+                    for (int pl = 1; pl < NP; pl++) {
+                        float w[32];
+                        tmem_ld32(trow + pl * h + c0, w);
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj++) v[jj] += w[jj];
+                    }
+                }
+            };
+            auto acc16 = [&](int c0, float(&v)[16]) {
+                tmem_ld16(trow + c0, v);
+                if (fused) {
+#pragma unroll
+                    for (int pl = 1; pl < NP; pl++) {
+                        float w[16];
+                        tmem_ld16(trow + pl * h + c0, w);
+#pragma unroll
+                        for (int jj = 0; jj < 16; jj++) v[jj] += w[jj];
+                    }
+                }
+            };
             if (PH == PH_UP) {
                 float mx = 0.f;
                 if (acc_ok) {
                     for (int c0 = 0; c0 < n; c0 += 32) {
                         float v[32];
-                        tmem_ld32(trow + c0, v);
+                        acc32(c0, v);
 #pragma unroll
                         for (int jj = 0; jj < 32; jj++) {
                             if (c0 + jj < n) {
@@ -1298,7 +1383,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 for (int c0 = 0; c0 < n; c0 += STG_COLS) {
                     if (acc_ok) {
                         float v[16];
-                        tmem_ld16(trow + c0, v);
+                        acc16(c0, v);
 #pragma unroll
                         for (int jj = 0; jj < STG_COLS; jj++) {
                             const float u = v[jj] * cs[(c0 + jj) & (NT - 1)];
@@ -1322,7 +1407,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
                 for (int c0 = 0; c0 < n; c0 += 32) {
                     float v[32];
-                    tmem_ld32(trow + c0, v);
+                    acc32(c0, v);
 #pragma unroll
                     for (int jj = 0; jj < 32; jj++)
                         if (c0 + jj < n) dst[(int64_t)(c0 + jj) * LAT] = v[jj] * cs[c0 + jj];
