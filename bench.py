@@ -109,9 +109,10 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def build_store(torch, S, dev, n_layers, seed):
-    """HBM-resident expert store: [n_layers*512, BLOCK] u8 in the T layout, s2 [n_layers, 512, 2],
-    per-layer m_hat and router, generated in batches on the device and converted with qmoe_to_T."""
+def build_store(torch, S, dev, n_layers, seed, layout_T=True):
+    """HBM-resident expert store: [n_layers*512, BLOCK] u8 in the T layout (converted with qmoe_to_T) or,
+    with layout_T=False, the orig layout; s2 [n_layers, 512, 2], per-layer m_hat and router, generated in
+    batches on the device."""
     import qmoe_ns as Q
     g = S.seeded(seed, dev)
     store = torch.empty(n_layers * NE, S.BLOCK, dtype=torch.uint8, device=dev)
@@ -128,7 +129,8 @@ def build_store(torch, S, dev, n_layers, seed):
             store[m * NE + e0:m * NE + e0 + B].copy_(blk)
             s2[m, e0:e0 + B] = s2b
             del blk
-        Q.to_T_batch(store[m * NE:(m + 1) * NE])
+        if layout_T:
+            Q.to_T_batch(store[m * NE:(m + 1) * NE])
     torch.cuda.synchronize()
     return store, s2, m_hats, routers, p_l
 
@@ -341,11 +343,15 @@ PREFILL_FLOP_PER_PAIR = 2 * (2688 * 1024 + 1024 * 2688)   # up + down MACs x 2 =
 
 
 def run_prefill(args):
-    """the prompt path, one MoE layer of 512 synthetic NVFP4 experts (T layout, 1.585 GB
-    resident in HBM), T tokens drawn as in config 0 and routed top-22 by the synthetic router; one step =
-    one qmoe_prefill_grouped call (routing sort, activation gather, up GEMM + ReLU^2, down GEMM, combine).
-    value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call with the
-    token block and routing copied from pinned host memory and the output copied back, every step."""
+    """the prompt path, one MoE layer of 512 synthetic NVFP4 experts (orig layout, the one
+    the reference's moe_pairs reads; 1.585 GB resident in HBM), T tokens drawn as in config 0 and routed
+    top-22 by the synthetic router; one step = one qmoe_prefill_grouped call: routing sort, x as NVFP4
+    planes, up GEMM + ReLU^2 (block-scaled NVFP4 tcgen05), h as NVFP4 planes, down GEMM, combine - 8
+    kernels. value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call
+    with the token block and routing copied from pinned host memory and the output copied back, every step.
+    roofline: the whole call against the slower of the HBM bound (weights of the experts hit + activations)
+    and the NVFP4 tensor bound (true FLOPs at 4x the measured dense bf16 rate, the FP4:bf16 ratio of the
+    tensor cores); `pipe_flop` counts the MMA work actually issued (three activation planes)."""
     import torch
     import qmoe_ns as Q
     import qmoe_synth as S
@@ -355,11 +361,11 @@ def run_prefill(args):
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             tpk = json.load(f)
-        tflops = float(tpk.get("bf16_tflops_sustained", tpk.get("bf16_tflops")))
-        tkind = "measured (cuBLAS bf16, sustained)"
+        tflops = 4.0 * float(tpk.get("bf16_tflops_sustained", tpk.get("bf16_tflops")))
+        tkind = "NVFP4 dense = 4 x measured cuBLAS bf16 (sustained)"
     except Exception:
-        tflops, tkind = 1400.0, "fallback"
-    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303)
+        tflops, tkind = 4.0 * 1400.0, "NVFP4 dense = 4 x fallback bf16 (sustained 1.4 PF)"
+    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303, layout_T=False)
     s2l = s2[0].contiguous()
     g = S.seeded(404, dev)
     T = args.prefill_t
@@ -372,7 +378,7 @@ def run_prefill(args):
     st = torch.cuda.Stream()
     with torch.cuda.stream(st):
         for _ in range(max(3, args.warmup)):
-            Q.moe_prefill(store, ids, w, s2l, X, out=out)
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=False, out=out)
         st.synchronize()
         if Q.prefill_status() != 0:
             raise RuntimeError("prefill kernels reported a device-side error")
@@ -382,7 +388,7 @@ def run_prefill(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for _ in range(args.steps):
-            Q.moe_prefill(store, ids, w, s2l, X, out=out)
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=False, out=out)
         e1.record(st)
         e1.synchronize()
         clocks = clk.stop()
@@ -401,7 +407,7 @@ def run_prefill(args):
             dx.copy_(hx, non_blocking=True)
             did.copy_(hid, non_blocking=True)
             dw.copy_(hw, non_blocking=True)
-            Q.moe_prefill(store, did, dw, s2l, dx, out=out)
+            Q.moe_prefill(store, did, dw, s2l, dx, layout_T=False, out=out)
             hout.copy_(out, non_blocking=True)
         e3.record(st)
         e3.synchronize()
@@ -420,26 +426,29 @@ def run_prefill(args):
                 "frac": round(t_tc / ms, 4), "peak_kind": tkind}
     roof["traffic"] = None
     roof["algorithmic"] = {"flop": flop, "weight_bytes": wbytes, "activation_bytes": act_bytes,
-                           "t_hbm_ms": round(t_hbm, 4), "t_tensor_ms": round(t_tc, 4)}
+                           "t_hbm_ms": round(t_hbm, 4), "t_tensor_ms": round(t_tc, 4),
+                           "pipe_flop": 3 * flop, "pipe_tflops": round(3 * flop / ms / 1e9, 1)}
     line = {"metric": "MoE prefill tokens/s (one routed-expert layer, top-22 of 512)", "value": round(T / ms * 1e3, 1),
             "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
             "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "nvfp4 x f16 -> f32 (tcgen05 kind::f16)", "data": "synthetic",
+            "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
+            "data": "synthetic",
             "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
-                       "unique_experts": uniq, "l2": "weights (1.585 GB) exceed L2"},
+                       "unique_experts": uniq, "layout": "orig", "l2": "weights (1.585 GB) exceed L2"},
             "roofline": roof, "clocks": clocks,
             "e2e": {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
-            "gpu_launches": 7 * args.steps}
+            "gpu_launches": 8 * args.steps}
     print(json.dumps(line), flush=True)
 
 
 def run_ep(args):
     """expert parallelism. The 512 experts of every layer are sharded over the N ranks
-    (expert e on rank e // (512 / N), T layout, resident in HBM); each rank holds a batch of --ep-t tokens.
+    (expert e on rank e // (512 / N), orig layout, resident in HBM); each rank holds a batch of --ep-t tokens.
     A step = `--layers` MoE layers, each an ExpertParallelMoE forward: dispatch pack, NCCL all_to_all of the
-    token blocks and routing, the local experts (grouped tcgen05 GEMM), all_to_all of the partial outputs,
+    token blocks and routing, the local experts (block-scaled NVFP4 tcgen05 grouped GEMM), all_to_all of
+    the partial outputs,
     rank-order combine. value = tokens of all ranks per second of max-over-ranks device time."""
     import datetime
     import torch
@@ -460,7 +469,7 @@ def run_ep(args):
     L, T = args.layers, args.ep_t
     el = NE // world
     g = S.seeded(1234, dev)
-    # this rank's experts of every layer (generated on the device, converted to the T layout)
+    # this rank's experts of every layer (generated on the device, orig layout)
     store = torch.empty(L * el, S.BLOCK, dtype=torch.uint8, device=dev)
     s2 = torch.empty(L, el, 2, dtype=torch.float32, device=dev)
     gl = S.seeded(99, dev)   # same m_hat / router on every rank
@@ -475,8 +484,8 @@ def run_ep(args):
             store[m * el + e0:m * el + e0 + nb].copy_(blk)
             s2[m, e0:e0 + nb] = s2b
             del blk
-        Q.to_T_batch(store[m * el:(m + 1) * el])
-    layers = [EP.ExpertParallelMoE(store[m * el:(m + 1) * el], s2[m], n_experts=NE) for m in range(L)]
+    layers = [EP.ExpertParallelMoE(store[m * el:(m + 1) * el], s2[m], n_experts=NE, layout_T=False)
+              for m in range(L)]
     gx = S.seeded(555 + rank, dev)
     X = [S.tokens(T, m_hats[m], gx, dev) for m in range(L)]
     R = [S.route(X[m], *routers[m]) for m in range(L)]
@@ -544,7 +553,7 @@ def run_ep(args):
                 "e2e": {"value": round(toks / me * 1e3, 1), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(L * T * (S.LAT * 2 + K * 12)),
                         "d2h_bytes_per_step": int(L * T * S.LAT * 4)},
-                "gpu_launches": L * args.steps * (2 + 7 + 1)}
+                "gpu_launches": L * args.steps * (2 + 8 + 1)}
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
