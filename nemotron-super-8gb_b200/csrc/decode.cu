@@ -1,12 +1,11 @@
 // Decode-step routed-expert kernels (bs = 1) for sm_100a.
 //
-//   decode_up_kernel    — `_up` (qmoe_ns.py:24-44): persistent CTAs; one producer thread streams 16-row
-//                         tiles (8 KB codes + 1 KB scales, both contiguous in the block) into a 16-stage
-//                         shared-memory ring with 1-D bulk copies (TMA engine) completing on mbarriers;
-//                         eight consumer warps each own whole tiles, keep their 32-element slice of x in
-//                         registers as prescaled f16x2, decode with cvt.e2m1x2 and reduce 16 rows with a
-//                         16-shuffle butterfly. Fused epilogue: ReLU^2, and the tile (= one 16-neuron group)
-//                         writes its 16-bit live-neuron mask, so no separate liveness pass is needed.
+//   decode_up_kernel    — `_up` (qmoe_ns.py:24-44): one CTA per SM, 16 warps; a warp takes whole 8-row tiles
+//                         and streams each row's 512 B of codes with 16-byte loads (a lane's 16 B of every
+//                         row of the tile in flight at once), keeps its 32-element slice of x in registers as
+//                         prescaled f16x2, decodes with cvt.e2m1x2, reduces the 8 rows with a 9-shuffle
+//                         butterfly. Fused epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask, so no
+//                         separate liveness pass is needed; live neurons' down rows are prefetched to L2.
 //   live_groups_kernel  — the torch glue of moe_decode_groups (qmoe_ns.py:249-251).
 //   decode_down_kernel  — `_down_groups` (qmoe_ns.py:209-239) over the T layout: CTA = (expert, split,
 //                         128-row chunk); compacts the live groups and live neurons into shared memory,
@@ -59,32 +58,89 @@ __device__ __forceinline__ void up_load(const uint8_t *base, int hg, int lane, U
     }
 }
 
-// `_up` (qmoe_ns.py:24-44) for bs = 1. One CTA per SM; warp w of CTA c takes tiles c + (w + 16k)*grid
-// (tile = 8 rows). A lane owns a 32-element slice of x (prescaled f16x2 in registers) and 16 bytes of
-// each row: it issues the 8 row loads of its tile at once, decodes the e2m1 codes with cvt.e2m1x2,
-// multiplies with HFMA2 per 16-element group, scales in fp32, and the 8 row partials are reduced with
-// a 9-shuffle butterfly. Epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask for the down
-// kernel. (Measured on B200: the 34 MB stream of one layer alone takes ~8.3 us per launch; software
-// pipelining the loads, claiming tiles dynamically, or more resident warps did not shorten it.)
-__global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
-    __shared__ const uint8_t *s_base[UP_MAXK];   // slot base of expert j (nullptr: slot out of range)
-    __shared__ float s_s2u[UP_MAXK];
-    __shared__ const uint8_t *s_tab[UP_MAXK];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = a.K * UP_HALVES;
-    // Launched as a programmatic dependent of the previous layer's kernels: everything below may read their
-    // outputs (sidx, x) or rewrite buffers they still read (the workspace counters), so wait first.
-    pdl_wait();
-    for (int j = threadIdx.x; j < a.K && j < UP_MAXK; j += blockDim.x) {
-        const int64_t slot = a.sidx[j];
-        s_base[j] = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
-        s_s2u[j] = a.s2[2 * j];
-        s_tab[j] = a.tab ? reinterpret_cast<const uint8_t *>(a.tab[j]) : nullptr;
+// One 8-row tile of `_up` (qmoe_ns.py:24-44) from a lane's share of its codes and scales: decode with
+// cvt.e2m1x2, HFMA2 per 16-element group against the prescaled x slice, fp32 group scaling, 9-shuffle
+// butterfly over the 8 rows, then ReLU^2, h, the tile's 8-bit live-neuron mask and the L2 prefetch of the
+// live neurons' down rows. Shared by both up kernels, so they give bit-identical h.
+__device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int j, int hg, float mult, bool bad,
+                                        const uint32_t (&xr)[16], int lane, const uint8_t *const *s_tab) {
+    float part[UP_ROWS];
+#pragma unroll
+    for (int r = 0; r < UP_ROWS; ++r) {
+        const uint4 w = cur.w[r];
+        __half2 a0 = __float2half2_rn(0.f), a1 = a0, b0 = a0, b1 = a0;
+        uint32_t o[4];
+        e2m1x8_f16x2(w.x, o);
+        a0 = __hfma2(as_h2(o[0]), as_h2(xr[0]), a0);
+        b0 = __hfma2(as_h2(o[1]), as_h2(xr[1]), b0);
+        a0 = __hfma2(as_h2(o[2]), as_h2(xr[2]), a0);
+        b0 = __hfma2(as_h2(o[3]), as_h2(xr[3]), b0);
+        e2m1x8_f16x2(w.y, o);
+        a0 = __hfma2(as_h2(o[0]), as_h2(xr[4]), a0);
+        b0 = __hfma2(as_h2(o[1]), as_h2(xr[5]), b0);
+        a0 = __hfma2(as_h2(o[2]), as_h2(xr[6]), a0);
+        b0 = __hfma2(as_h2(o[3]), as_h2(xr[7]), b0);
+        e2m1x8_f16x2(w.z, o);
+        a1 = __hfma2(as_h2(o[0]), as_h2(xr[8]), a1);
+        b1 = __hfma2(as_h2(o[1]), as_h2(xr[9]), b1);
+        a1 = __hfma2(as_h2(o[2]), as_h2(xr[10]), a1);
+        b1 = __hfma2(as_h2(o[3]), as_h2(xr[11]), b1);
+        e2m1x8_f16x2(w.w, o);
+        a1 = __hfma2(as_h2(o[0]), as_h2(xr[12]), a1);
+        b1 = __hfma2(as_h2(o[1]), as_h2(xr[13]), b1);
+        a1 = __hfma2(as_h2(o[2]), as_h2(xr[14]), a1);
+        b1 = __hfma2(as_h2(o[3]), as_h2(xr[15]), b1);
+        const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(cur.sc[r])));
+        const float2 fa = __half22float2(__hadd2(a0, b0));   // group 2*lane
+        const float2 fb = __half22float2(__hadd2(a1, b1));   // group 2*lane+1
+        part[r] = (fa.x + fa.y) * sf.x + (fb.x + fb.y) * sf.y;
     }
-    if (blockIdx.x == 0 && a.zero_words && (int)threadIdx.x < a.nzero) a.zero_words[threadIdx.x] = 0;
-    __syncthreads();
-    pdl_launch_dependents();
+    // butterfly: 8 row partials over 32 lanes -> lanes 4r..4r+3 hold row r
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const bool up = lane & 16;
+        const float send = up ? part[i] : part[i + 4];
+        part[i] = (up ? part[i + 4] : part[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const bool up = lane & 8;
+        const float send = up ? part[i] : part[i + 2];
+        part[i] = (up ? part[i + 2] : part[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
+    }
+    {
+        const bool up = lane & 4;
+        const float send = up ? part[0] : part[1];
+        part[0] = (up ? part[1] : part[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+    }
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], 2);
+    part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
 
+    const float u = fmaxf(part[0] * mult, 0.f);   // ReLU^2 (qmoe_ns.py:42-44)
+    float hv = u * u;
+    if (bad) hv = __int_as_float(0x7fc00000);
+    const bool lead = (lane & 3) == 0;
+    if (lead) a.h[(int64_t)j * INTER + hg * UP_ROWS + (lane >> 2)] = hv;
+    if (a.gmask8 || a.tab) {
+        const unsigned m = __reduce_or_sync(0xffffffffu, (lead && (hv > 0.f || bad)) ? (1u << (lane >> 2)) : 0u);
+        if (a.gmask8 && lane == 0) a.gmask8[(int64_t)j * UP_HALVES + hg] = (uint8_t)m;
+        // The down kernel reads, per live neuron, its 512-byte row of dnT_w and, per live group, the
+        // group's 1024-byte row of dnT_s: start bringing them into L2 now, while the up stream runs.
+        const uint8_t *tb = a.tab ? (j < UP_MAXK ? s_tab[j] : reinterpret_cast<const uint8_t *>(a.tab[j])) : nullptr;
+        if (tb && !bad && m) {
+            if (lead && hv > 0.f) {
+                const uint8_t *row = tb + O_DW + (int64_t)(hg * UP_ROWS + (lane >> 2)) * (LAT / 2);
+#pragma unroll
+                for (int l = 0; l < 4; ++l) prefetch_l2(row + 128 * l);
+            }
+            if (lane >= 24) prefetch_l2(tb + O_DS + (int64_t)(hg >> 1) * LAT + 128 * (lane - 24));
+        }
+    }
+}
+
+// A lane's 32-element slice [32*lane, 32*lane+32) of x as f16x2, scaled by 2^E (amax*2^E in [256, 512), so
+// each 16-element group sum of exact e2m1*x products stays below 2^16); inv = 2^-E.
+__device__ __forceinline__ void up_prep_x(const UpArgs &a, int lane, uint32_t (&xr)[16], float &inv) {
     // x slice [32*lane, 32*lane+32) as f16x2 scaled by 2^E: amax*2^E in [256, 512), so each
     // 16-element group sum of exact e2m1*x products stays below 2^16
     float xv[32];
@@ -111,11 +167,41 @@ __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
     for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     const int E = prescale_exp(am, 9);
     const float pe = pow2f(E);
-    uint32_t xr[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k)
         xr[k] = h2_as_u(__halves2half2(__float2half_rn(xv[2 * k] * pe), __float2half_rn(xv[2 * k + 1] * pe)));
-    const float inv = pow2f(-E);
+    inv = pow2f(-E);
+}
+
+// `_up` (qmoe_ns.py:24-44) for bs = 1. One CTA per SM; warp w of CTA c takes tiles c + (w + 16k)*grid
+// (tile = 8 rows). A lane owns a 32-element slice of x (prescaled f16x2 in registers) and 16 bytes of
+// each row: it issues the 8 row loads of its tile at once, decodes the e2m1 codes with cvt.e2m1x2,
+// multiplies with HFMA2 per 16-element group, scales in fp32, and the 8 row partials are reduced with
+// a 9-shuffle butterfly. Epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask for the down
+// kernel. (Measured on B200: the 34 MB stream of one layer alone takes ~8.3 us per launch; software
+// pipelining the loads, claiming tiles dynamically, or more resident warps did not shorten it.)
+__global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
+    __shared__ const uint8_t *s_base[UP_MAXK];   // slot base of expert j (nullptr: slot out of range)
+    __shared__ float s_s2u[UP_MAXK];
+    __shared__ const uint8_t *s_tab[UP_MAXK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = a.K * UP_HALVES;
+    // Launched as a programmatic dependent of the previous layer's kernels: everything below may read their
+    // outputs (sidx, x) or rewrite buffers they still read (the workspace counters), so wait first.
+    pdl_wait();
+    for (int j = threadIdx.x; j < a.K && j < UP_MAXK; j += blockDim.x) {
+        const int64_t slot = a.sidx[j];
+        s_base[j] = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
+        s_s2u[j] = a.s2[2 * j];
+        s_tab[j] = a.tab ? reinterpret_cast<const uint8_t *>(a.tab[j]) : nullptr;
+    }
+    if (blockIdx.x == 0 && a.zero_words && (int)threadIdx.x < a.nzero) a.zero_words[threadIdx.x] = 0;
+    __syncthreads();
+    pdl_launch_dependents();
+
+    uint32_t xr[16];
+    float inv;
+    up_prep_x(a, lane, xr, inv);
 
     for (int t = blockIdx.x + warp * gridDim.x; t < ntiles; t += UP_NW * gridDim.x) {
         const int j = t / UP_HALVES, hg = t - j * UP_HALVES;
@@ -132,80 +218,10 @@ __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
         const bool bad = base == nullptr;
         UpTile cur;
         if (!bad) up_load(base, hg, lane, cur);
-        float part[UP_ROWS];
-#pragma unroll
-        for (int r = 0; r < UP_ROWS; ++r) {
-            const uint4 w = cur.w[r];
-            __half2 a0 = __float2half2_rn(0.f), a1 = a0, b0 = a0, b1 = a0;
-            uint32_t o[4];
-            e2m1x8_f16x2(w.x, o);
-            a0 = __hfma2(as_h2(o[0]), as_h2(xr[0]), a0);
-            b0 = __hfma2(as_h2(o[1]), as_h2(xr[1]), b0);
-            a0 = __hfma2(as_h2(o[2]), as_h2(xr[2]), a0);
-            b0 = __hfma2(as_h2(o[3]), as_h2(xr[3]), b0);
-            e2m1x8_f16x2(w.y, o);
-            a0 = __hfma2(as_h2(o[0]), as_h2(xr[4]), a0);
-            b0 = __hfma2(as_h2(o[1]), as_h2(xr[5]), b0);
-            a0 = __hfma2(as_h2(o[2]), as_h2(xr[6]), a0);
-            b0 = __hfma2(as_h2(o[3]), as_h2(xr[7]), b0);
-            e2m1x8_f16x2(w.z, o);
-            a1 = __hfma2(as_h2(o[0]), as_h2(xr[8]), a1);
-            b1 = __hfma2(as_h2(o[1]), as_h2(xr[9]), b1);
-            a1 = __hfma2(as_h2(o[2]), as_h2(xr[10]), a1);
-            b1 = __hfma2(as_h2(o[3]), as_h2(xr[11]), b1);
-            e2m1x8_f16x2(w.w, o);
-            a1 = __hfma2(as_h2(o[0]), as_h2(xr[12]), a1);
-            b1 = __hfma2(as_h2(o[1]), as_h2(xr[13]), b1);
-            a1 = __hfma2(as_h2(o[2]), as_h2(xr[14]), a1);
-            b1 = __hfma2(as_h2(o[3]), as_h2(xr[15]), b1);
-            const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(cur.sc[r])));
-            const float2 fa = __half22float2(__hadd2(a0, b0));   // group 2*lane
-            const float2 fb = __half22float2(__hadd2(a1, b1));   // group 2*lane+1
-            part[r] = (fa.x + fa.y) * sf.x + (fb.x + fb.y) * sf.y;
-        }
-        // butterfly: 8 row partials over 32 lanes -> lanes 4r..4r+3 hold row r
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const bool up = lane & 16;
-            const float send = up ? part[i] : part[i + 4];
-            part[i] = (up ? part[i + 4] : part[i]) + __shfl_xor_sync(0xffffffffu, send, 16);
-        }
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-            const bool up = lane & 8;
-            const float send = up ? part[i] : part[i + 2];
-            part[i] = (up ? part[i + 2] : part[i]) + __shfl_xor_sync(0xffffffffu, send, 8);
-        }
-        {
-            const bool up = lane & 4;
-            const float send = up ? part[0] : part[1];
-            part[0] = (up ? part[1] : part[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
-        }
-        part[0] += __shfl_xor_sync(0xffffffffu, part[0], 2);
-        part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
-
-        const float u = fmaxf(part[0] * mult, 0.f);   // ReLU^2 (qmoe_ns.py:42-44)
-        float hv = u * u;
-        if (bad) hv = __int_as_float(0x7fc00000);
-        const bool lead = (lane & 3) == 0;
-        if (lead) a.h[(int64_t)j * INTER + hg * UP_ROWS + (lane >> 2)] = hv;
-        if (a.gmask8 || a.tab) {
-            const unsigned m = __reduce_or_sync(0xffffffffu, (lead && (hv > 0.f || bad)) ? (1u << (lane >> 2)) : 0u);
-            if (a.gmask8 && lane == 0) a.gmask8[(int64_t)j * UP_HALVES + hg] = (uint8_t)m;
-            // The down kernel reads, per live neuron, its 512-byte row of dnT_w and, per live group, the
-            // group's 1024-byte row of dnT_s: start bringing them into L2 now, while the up stream runs.
-            const uint8_t *tb = a.tab ? (j < UP_MAXK ? s_tab[j] : reinterpret_cast<const uint8_t *>(a.tab[j])) : nullptr;
-            if (tb && !bad && m) {
-                if (lead && hv > 0.f) {
-                    const uint8_t *row = tb + O_DW + (int64_t)(hg * UP_ROWS + (lane >> 2)) * (LAT / 2);
-#pragma unroll
-                    for (int l = 0; l < 4; ++l) prefetch_l2(row + 128 * l);
-                }
-                if (lane >= 24) prefetch_l2(tb + O_DS + (int64_t)(hg >> 1) * LAT + 128 * (lane - 24));
-            }
-        }
+        up_tile(a, cur, j, hg, mult, bad, xr, lane, s_tab);
     }
 }
+
 
 // ------------------------------------------------------------------ live groups (qmoe_ns.py:249-251)
 __global__ void __launch_bounds__(192) live_groups_kernel(const float *__restrict__ h, int32_t *__restrict__ gidx,
