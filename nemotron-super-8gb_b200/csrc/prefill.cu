@@ -821,7 +821,7 @@ struct BsPlan {
     static constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;
     static constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;
     static constexpr int OFF_BAR = OFF_RED + 32;
-    static constexpr int NBAR = 3 * STAGES + 8;
+    static constexpr int NBAR = 4 * STAGES + 8;
     static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
     static constexpr int OFF_ABORT = OFF_TMEM + 16;
     static constexpr int SMEM = OFF_ABORT + 16 + 1024;
@@ -1081,13 +1081,15 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *slab_full = acc_empty + 2;
     uint64_t *sf_full = slab_full + 2;   // [S] the stage's scale factors are in TMEM (all four store warps)
+    uint64_t *sf_src = sf_full + S;      // [S] the stage's scale atoms are in shared memory (bulk copy + weight atoms)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 3);   // A and B expect_tx arrivals, the weight-atom warp
+            mbar_init(&full[s], 2);     // A and B expect_tx arrivals (codes)
+            mbar_init(&sf_src[s], 2);   // B issuer's expect_tx for the planes' atoms, the weight-atom warp
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; a++) {
@@ -1157,9 +1159,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2) + BS_SFB));
+                    // the atoms first, on their own barrier: the scale stores into TMEM need not wait for codes
+                    mbar_expect_tx(&sf_src[s], (uint32_t)BS_SFB);
+                    bulk_g2s_nohint(sm + s * BS_STAGE + BS_A + BS_B, sfb_tile + (int64_t)kt * BS_SFB, BS_SFB, &sf_src[s]);
+                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2)));
                     tma_load_3d(sm + s * BS_STAGE + BS_A, map, kt * (BS_BK / 2), n0, 0, &full[s]);
-                    bulk_g2s_nohint(sm + s * BS_STAGE + BS_A + BS_B, sfb_tile + (int64_t)kt * BS_SFB, BS_SFB, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -1215,9 +1219,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B + BS_SFB;
                 *reinterpret_cast<uint4 *>(at + lane * 16) = make_uint4(w[0].x, w[1].x, w[2].x, w[3].x);
                 *reinterpret_cast<uint4 *>(at + BS_ATOM + lane * 16) = make_uint4(w[0].y, w[1].y, w[2].y, w[3].y);
-                fence_async_smem();   // generic-proxy atom stores -> visible to tcgen05.cp
+                fence_async_smem();   // generic-proxy atom stores, ordered before the async proxy's next use
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+                if (lane == 0) mbar_arrive(&sf_src[s]);
             }
             if (!ok) break;
         }
@@ -1278,8 +1282,8 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         // ------------------------------------------------------------ scale-factor atoms -> TMEM slot of the stage
         // tcgen05.st from four warps, warp w writing lane quarter w % 4: each quarter gets the 32-row pattern of
         // every atom (lane L, column c = bytes 16L + 4c .. 16L + 4c + 3), the layout a 32x128b.warpx4 copy
-        // makes, without occupying the tensor pipe. Slot s is rewritten only after full[s] of its next use,
-        // which follows empty[s] (the MMAs that read the slot completed) through the producers.
+        // makes, without occupying the tensor pipe. Slot s is rewritten only after sf_src[s] of its next use,
+        // which follows empty[s] (the MMAs that read the slot completed) through its producers.
         const uint32_t quarter = (uint32_t)(warp & 3) << 21;   // TMEM lane 32 * (warp % 4), in bits 16..
         uint32_t q = 0;
         for (int i = blockIdx.x; i < nitems; i += gridDim.x) {
@@ -1287,11 +1291,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             bool ok = true;
             for (int kt = 0; kt < NST; kt++, q++) {
                 const int s = q % S;
-                if (!warp_wait_bo(&full[s], (q / S) & 1, lane, abort_flag, p.status)) {
+                if (!warp_wait_bo(&sf_src[s], (q / S) & 1, lane, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
-                mbar_try_wait(&full[s], (q / S) & 1);   // completed phase: acquire for every lane
+                mbar_try_wait(&sf_src[s], (q / S) & 1);   // completed phase: acquire for every lane
                 const uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B;
 #pragma unroll
                 for (int kk = 0; kk < BS_KS; kk++) {
