@@ -1,0 +1,108 @@
+"""The whole Nemotron-H MoE layer of a decode step on the device, without host synchronisation, and a
+multi-layer step captured as one CUDA graph.
+
+The reference's decode MoE (`moe_forward`, nem_super.py:358-392) must stop on the host once per layer
+(`.tolist()` of the routed ids, :371) to drive its NVMe/RAM expert cache. With every expert resident in HBM
+(expert_store.ExpertStore) nothing needs the ids on the host, so the layer is the stock
+NemotronHMoE.forward (tf:722-737) over device-side parts:
+
+    logits = x @ gate^T (fp32, tf:748-751) -> sigmoid + correction bias -> top-k ids, weights (tf:697-720)
+    lat = fc1_latent_proj(x)                                     (dense_q GEMV: FP8 / NVFP4 / bf16)
+    y   = routed experts(lat, ids, weights)                      (RoutedExperts: moe_decode_groups)
+    out = fc2_latent_proj(y) + shared_down(relu(shared_up(x))^2) (dense_q GEMVs)
+
+`MoELayer.forward` runs it eagerly; `DecodeGraph` records the layers of a step once as a CUDA graph over
+static input/output buffers and replays it per token (one launch for the whole step).
+"""
+import torch
+import torch.nn.functional as F
+
+import dense_q as D
+from expert_store import RoutedExperts
+
+
+def linear(w, x):
+    """x [..., K] -> [..., N] in x.dtype: a dense_q quantized-weight dict (FP8 / NVFP4, dense_q.py:237-247)
+    runs the B200 GEMV kernels; a plain [N, K] tensor runs F.linear."""
+    if isinstance(w, dict):
+        return D.qlinear(w, x)
+    return F.linear(x, w.to(x.dtype))
+
+
+def route_tokens(x, gate_w, bias, top_k=22, scaling=5.0, n_group=1, topk_group=1, norm_topk_prob=False):
+    """tf:748-751 + tf:697-720 (NemotronHTopkRouter.forward, NemotronHMoE.route_tokens_to_experts) as torch
+    ops on the device: x [T, hidden] -> ids int64 [T, top_k], weights f32 [T, top_k]."""
+    logits = F.linear(x.reshape(-1, x.shape[-1]).to(torch.float32), gate_w.to(torch.float32))
+    scores = logits.sigmoid()
+    choice = scores + bias
+    if n_group > 1:
+        n = choice.shape[-1]
+        group_scores = choice.view(-1, n_group, n // n_group).topk(2, dim=-1)[0].sum(dim=-1)
+        group_idx = torch.topk(group_scores, k=topk_group, dim=-1, sorted=False)[1]
+        group_mask = torch.zeros_like(group_scores)
+        group_mask.scatter_(1, group_idx, 1)
+        score_mask = group_mask.unsqueeze(-1).expand(-1, n_group, n // n_group).reshape(-1, n)
+        choice = choice.masked_fill(~score_mask.bool(), 0.0)
+    ids = torch.topk(choice, k=top_k, dim=-1, sorted=False)[1]
+    w = scores.gather(1, ids)
+    if norm_topk_prob:
+        w = w / (w.sum(dim=-1, keepdim=True) + 1e-20)
+    return ids, w * scaling
+
+
+class MoELayer(torch.nn.Module):
+    """One NemotronHMoE layer m (tf:663-737): gate_w [512, hidden] and bias [512] (router), fc1 [1024, hidden]
+    and fc2 [hidden, 1024] (latent projections), shared_up [I, hidden] and shared_down [hidden, I] (shared
+    expert, relu^2), each a dense_q dict or a plain weight; the routed experts from `store`."""
+
+    def __init__(self, m, store, gate_w, bias, fc1, fc2, shared_up, shared_down, top_k=22, scaling=5.0,
+                 n_group=1, topk_group=1, norm_topk_prob=False):
+        super().__init__()
+        self.gate_w, self.bias = gate_w, bias
+        self.fc1, self.fc2, self.shared_up, self.shared_down = fc1, fc2, shared_up, shared_down
+        self.route_args = dict(top_k=top_k, scaling=scaling, n_group=n_group, topk_group=topk_group,
+                               norm_topk_prob=norm_topk_prob)
+        self.experts = RoutedExperts(m, store, topk=top_k)
+
+    def forward(self, hidden_states):
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1])
+        ids, w = route_tokens(x, self.gate_w, self.bias, **self.route_args)
+        lat = linear(self.fc1, x)
+        y = self.experts(lat, ids, w)
+        out = linear(self.fc2, y)
+        u = torch.relu(linear(self.shared_up, x))
+        out = out + linear(self.shared_down, u * u)
+        return out.view(shape)
+
+
+class DecodeGraph:
+    """The layers of one decode step (a token through every MoE layer in order, each layer's output feeding
+    the next) recorded once as a CUDA graph: replay(x) copies x [1, hidden] into the static input, replays,
+    and returns the static output buffer (valid until the next replay). Warm-up runs before capture so
+    that every workspace and library handle exists before recording."""
+
+    def __init__(self, layers, hidden, dtype=torch.bfloat16, device="cuda", warmup=2):
+        self.layers = layers
+        self.x = torch.zeros(1, hidden, dtype=dtype, device=device)
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(s):
+            for _ in range(warmup):
+                self._run()
+        torch.cuda.current_stream(device).wait_stream(s)
+        torch.cuda.synchronize(device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):   # the warm-up stream: its workspaces are reused
+            self.out = self._run()
+
+    def _run(self):
+        h = self.x
+        for layer in self.layers:
+            h = layer(h)
+        return h
+
+    def replay(self, x):
+        self.x.copy_(x.reshape(self.x.shape))
+        self.graph.replay()
+        return self.out

@@ -95,6 +95,24 @@ class ExpertStore:
         if self.device.type == "cuda":
             torch.cuda.current_stream(self.device).synchronize()
 
+    @classmethod
+    def from_tensors(cls, blocks, s2, layout, layers=None, shard=None, n_experts=N_EXPERTS):
+        """A store over blocks already on the device (e.g. generated, or read by other means): blocks
+        [L * E_local, BLOCK] u8 in `layout`, s2 [L, E_local, 2] f32; no file is read."""
+        st = cls.__new__(cls)
+        L = s2.shape[0]
+        st.directory, st.device, st.n_experts = None, blocks.device, n_experts
+        st.layers = list(range(L)) if layers is None else [int(m) for m in layers]
+        st.lo, st.hi = (0, n_experts) if shard is None else (int(shard[0]), int(shard[1]))
+        st.e_local = st.hi - st.lo
+        if blocks.dtype != torch.uint8 or tuple(blocks.shape) != (L * st.e_local, Q.BLOCK) or len(st.layers) != L:
+            raise ValueError("blocks must be uint8 [L * E_local, BLOCK] matching s2 [L, E_local, 2] and layers")
+        if layout not in ("T", "orig"):
+            raise ValueError("layout must be 'T' or 'orig'")
+        st.file_layout = st.layout = layout
+        st.blocks, st.s2 = blocks, s2.to(torch.float32).contiguous()
+        return st
+
     # ------------------------------------------------------------------ loading
     def _runs(self, chunk_blocks):
         """(file block index, store row, count) runs of at most chunk_blocks contiguous blocks."""
