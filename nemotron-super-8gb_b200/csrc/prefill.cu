@@ -807,7 +807,17 @@ constexpr int BS_SFB = BS_KS * NP * BS_ATOM;   // 3 KB: the planes' atoms of a s
 constexpr int BS_SFA = BS_KS * BS_ATOM;        // 1 KB: the weights' atoms of a stage
 constexpr int BS_STAGE = BS_A + BS_B + BS_SFB + BS_SFA;
 constexpr int KS_UP = LAT / 64, KS_DN = INTER / 64;   // MMA k-steps of a row: 16 (up), 42 (down)
+// Wide stages: a tile of h <= 32 pair rows (its planes run as one MMA) moves 256 k-elements per stage in the
+// same 36 KB - weights [2 halves][128 rows][64 B] at 0, planes [2][NP][h][64 B] at 16 KB, plane atoms
+// [4 k-steps][NP][512 B] at 28 KB, weight atoms [4][512 B] at 34 KB - so twice the weight bytes are in
+// flight per stage and the per-stage hand-offs are paid once per 256. Other tiles use 128-element stages
+// laid out as A | B | plane atoms | weight atoms (BS_A, BS_B, BS_SFB, BS_SFA).
+constexpr int BW_B = 2 * BS_A;
+constexpr int BW_SFB = BW_B + 2 * NP * 32 * (BS_BK / 2);
+constexpr int BW_SFA = BW_SFB + 2 * BS_SFB;
 static_assert(BS_STAGE % 1024 == 0 && BS_A % 512 == 0, "TMA destinations and swizzle atoms");
+static_assert(BW_SFA + 2 * BS_SFA == BS_STAGE && BW_B % 512 == 0 && (NP * 16 * (BS_BK / 2)) % 512 == 0,
+              "a wide stage fills the stage; its plane halves start on 64-byte swizzle atoms");
 
 // Shared-memory plan of pfb_gemm_kernel<PH>: the stage ring, two slabs of the item's weight scales (128 rows
 // x all of K: 8 KB up, 21 KB down), epilogue staging, barriers. The down half's larger slabs leave room for
@@ -1117,21 +1127,26 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         const int pr = warp - BS_W_A;
         if (lane == 0) {
             uint32_t q = 0;
-            int e_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].x : 0;
+            int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
             for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
-                const int mt = i % MT, e = e_next;
-                if (i + (int)gridDim.x < nitems) e_next = p.tiles[(i + gridDim.x) / MT].x;
+                const int4 td = td_next;
+                if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
+                const int mt = i % MT, e = td.x;
+                const bool wide = fused_planes(b_rows(td.z));
+                const int nst = wide ? (NST + 1) / 2 : NST;
                 bool ok = true;
-                for (int kt = 0; kt < NST; kt++, q++) {
+                for (int kt = 0; kt < nst; kt++, q++) {
                     if ((int)(q % BS_NA) != pr) continue;
                     const int s = q % S;
                     if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[s], BS_A);
-                    tma_load_3d(sm + s * BS_STAGE, &tm_w, kt * (BS_BK / 2), (PH == PH_UP ? 0 : ROW1344_DW) + mt * BM, e,
-                                &full[s]);
+                    const int nh = wide ? min(2, NST - 2 * kt) : 1, k0 = wide ? 2 * kt : kt;
+                    mbar_expect_tx(&full[s], (uint32_t)(nh * BS_A));
+                    for (int hh = 0; hh < nh; hh++)
+                        tma_load_3d(sm + s * BS_STAGE + hh * BS_A, &tm_w, (k0 + hh) * (BS_BK / 2),
+                                    (PH == PH_UP ? 0 : ROW1344_DW) + mt * BM, e, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -1151,19 +1166,27 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const int n0 = td.y, np_ = b_rows(td.z);
                 const CUtensorMap *map = np_ == 16 ? &tm_b16 : np_ == 32 ? &tm_b32 : np_ == 64 ? &tm_b64 : &tm_b128;
                 const uint8_t *sfb_tile = sfb + (int64_t)(i / MT) * KS * NP * BS_ATOM;
+                const bool wide = fused_planes(np_);
+                const int nst = wide ? (NST + 1) / 2 : NST;
+                const int pbytes = NP * np_ * (BS_BK / 2);   // one 128-element half of the planes
                 bool ok = true;
-                for (int kt = 0; kt < NST; kt++, q++) {
+                for (int kt = 0; kt < nst; kt++, q++) {
                     if ((int)(q % BS_NB) != pb) continue;
                     const int s = q % S;
                     if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
+                    const int nh = wide ? min(2, NST - 2 * kt) : 1, k0 = wide ? 2 * kt : kt;
+                    uint8_t *st = sm + s * BS_STAGE;
                     // the atoms first, on their own barrier: the scale stores into TMEM need not wait for codes
-                    mbar_expect_tx(&sf_src[s], (uint32_t)BS_SFB);
-                    bulk_g2s_nohint(sm + s * BS_STAGE + BS_A + BS_B, sfb_tile + (int64_t)kt * BS_SFB, BS_SFB, &sf_src[s]);
-                    mbar_expect_tx(&full[s], (uint32_t)(NP * np_ * (BS_BK / 2)));
-                    tma_load_3d(sm + s * BS_STAGE + BS_A, map, kt * (BS_BK / 2), n0, 0, &full[s]);
+                    mbar_expect_tx(&sf_src[s], (uint32_t)(nh * BS_SFB));
+                    bulk_g2s_nohint(st + (wide ? BW_SFB : BS_A + BS_B), sfb_tile + (int64_t)k0 * BS_SFB,
+                                    (uint32_t)(nh * BS_SFB), &sf_src[s]);
+                    mbar_expect_tx(&full[s], (uint32_t)(nh * pbytes));
+                    for (int hh = 0; hh < nh; hh++)
+                        tma_load_3d(st + (wide ? BW_B + hh * pbytes : BS_A), map, (k0 + hh) * (BS_BK / 2), n0, 0,
+                                    &full[s]);
                 }
                 if (!ok) break;
             }
@@ -1206,19 +1229,25 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             mbar_try_wait(&slab_full[b], (j >> 1) & 1);   // completed phase: acquire for every lane
             done[b]++;
             const uint8_t *sl = slab + b * Plan::SLAB;
+            const bool wide = fused_planes(b_rows(p.tiles[i / MT].z));
+            const int nst = wide ? (NST + 1) / 2 : NST;
             bool ok = true;
-            for (int kt = 0; kt < NST; kt++, q++) {
+            for (int kt = 0; kt < nst; kt++, q++) {
                 const int s = q % S;
                 if (!warp_wait_bo(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
-                uint2 w[4];
+                const int nh = wide ? min(2, NST - 2 * kt) : 1, k0 = wide ? 2 * kt : kt;
+                uint8_t *at = sm + s * BS_STAGE + (wide ? BW_SFA : BS_A + BS_B + BS_SFB);
+                for (int hh = 0; hh < nh; hh++) {   // 128-element half: k-steps 2(k0+hh), 2(k0+hh)+1
+                    uint2 w[4];
 #pragma unroll
-                for (int g = 0; g < 4; g++) w[g] = *reinterpret_cast<const uint2 *>(sl + (lane + 32 * g) * GP + 8 * kt);
-                uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B + BS_SFB;
-                *reinterpret_cast<uint4 *>(at + lane * 16) = make_uint4(w[0].x, w[1].x, w[2].x, w[3].x);
-                *reinterpret_cast<uint4 *>(at + BS_ATOM + lane * 16) = make_uint4(w[0].y, w[1].y, w[2].y, w[3].y);
+                    for (int g = 0; g < 4; g++)
+                        w[g] = *reinterpret_cast<const uint2 *>(sl + (lane + 32 * g) * GP + 8 * (k0 + hh));
+                    *reinterpret_cast<uint4 *>(at + (2 * hh) * BS_ATOM + lane * 16) = make_uint4(w[0].x, w[1].x, w[2].x, w[3].x);
+                    *reinterpret_cast<uint4 *>(at + (2 * hh + 1) * BS_ATOM + lane * 16) = make_uint4(w[0].y, w[1].y, w[2].y, w[3].y);
+                }
                 fence_async_smem();   // generic-proxy atom stores, ordered before the async proxy's next use
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sf_src[s]);
@@ -1246,8 +1275,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 tc_fence_after();
                 const uint32_t idesc = instr_desc_nvfp4(fused ? NP * np_ : (n + 15) & ~15);
                 const uint32_t d = tmem + a * NT;
+                const int nst = fused ? (NST + 1) / 2 : NST;   // fused tiles use wide stages
                 bool ok = true;
-                for (int kt = 0; kt < NST; kt++, q++) {
+                for (int kt = 0; kt < nst; kt++, q++) {
                     const int s = q % S;
                     if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status) ||
                         !lane_wait(&sf_full[s], (q / S) & 1, abort_flag, p.status)) {
@@ -1256,14 +1286,20 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t st0 = sbase + s * BS_STAGE;
+                    const uint32_t slot = tmem + BS_SF_COL + s * 32;
+                    if (fused) {   // all planes as one MMA: N = NP * np_ rows of B, scales in the plane-0 atom
+                        const int nk = 2 * min(2, NST - 2 * kt);
+                        for (int kk = 0; kk < nk; kk++) {
+                            const uint32_t half = (uint32_t)(kk >> 1), kb = (uint32_t)(kk & 1) * 32;
+                            const uint64_t ad = smem_desc(st0 + half * BS_A + kb, 16, 512, 4);
+                            const uint64_t bd = smem_desc(st0 + BW_B + half * (NP * np_ * (BS_BK / 2)) + kb, 16, 512, 4);
+                            mma_nvfp4(d, ad, bd, idesc, (kt | kk) != 0, slot + kk * 8, slot + kk * 8 + 4);
+                        }
+                    } else {
 #pragma unroll
-                    for (int kk = 0; kk < BS_KS; kk++) {
-                        const uint32_t sfa = tmem + BS_SF_COL + s * 32 + kk * 16;
-                        const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
-                        if (fused) {   // all planes: N = NP * np_ rows of B, scales in the plane-0 atom
-                            const uint64_t bd = smem_desc(st0 + BS_A + kk * 32, 16, 512, 4);
-                            mma_nvfp4(d, ad, bd, idesc, (kt | kk) != 0, sfa, sfa + 4);
-                        } else {
+                        for (int kk = 0; kk < BS_KS; kk++) {
+                            const uint32_t sfa = slot + kk * 16;
+                            const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
 #pragma unroll
                             for (int pl = 0; pl < NP; pl++) {
                                 const uint64_t bd = smem_desc(st0 + BS_A + pl * np_ * (BS_BK / 2) + kk * 32, 16, 512, 4);
@@ -1288,14 +1324,38 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         uint32_t q = 0;
         for (int i = blockIdx.x; i < nitems; i += gridDim.x) {
             if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;   // one decision for the whole warp
+            const bool wide = fused_planes(b_rows(p.tiles[i / MT].z));
+            const int nst = wide ? (NST + 1) / 2 : NST;
             bool ok = true;
-            for (int kt = 0; kt < NST; kt++, q++) {
+            for (int kt = 0; kt < nst; kt++, q++) {
                 const int s = q % S;
                 if (!warp_wait_bo(&sf_src[s], (q / S) & 1, lane, abort_flag, p.status)) {
                     ok = false;
                     break;
                 }
                 mbar_try_wait(&sf_src[s], (q / S) & 1);   // completed phase: acquire for every lane
+                if (wide) {
+                    // per k-step kk: columns 8kk .. 8kk+3 weight atom, 8kk+4 .. 8kk+7 the plane-0 (all-plane) atom
+                    const uint8_t *at = sm + s * BS_STAGE;
+                    const int nh = min(2, NST - 2 * kt);
+                    for (int hh = 0; hh < nh; hh++) {
+                        uint32_t r[16];
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {
+                            const int kk = 2 * hh + u;
+                            const uint4 a = *reinterpret_cast<const uint4 *>(at + BW_SFA + kk * BS_ATOM + lane * 16);
+                            const uint4 b = *reinterpret_cast<const uint4 *>(at + BW_SFB + kk * NP * BS_ATOM + lane * 16);
+                            r[8 * u + 0] = a.x, r[8 * u + 1] = a.y, r[8 * u + 2] = a.z, r[8 * u + 3] = a.w;
+                            r[8 * u + 4] = b.x, r[8 * u + 5] = b.y, r[8 * u + 6] = b.z, r[8 * u + 7] = b.w;
+                        }
+                        tmem_st16(tmem + quarter + BS_SF_COL + s * 32 + hh * 16, r);
+                    }
+                    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sf_full[s]);
+                    continue;
+                }
                 const uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B;
 #pragma unroll
                 for (int kk = 0; kk < BS_KS; kk++) {
