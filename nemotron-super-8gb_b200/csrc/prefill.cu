@@ -103,7 +103,8 @@ struct Params {
     int *pair_exp;          // [P]
     int *tile_scale;        // [tiles_cap, 21]
     __half *xp;             // [P, 1024]
-    __half *hs;             // [P, 2688]
+    __half *hs;             // [P, 2688] f16 x 2^S_b per 128-row block (T layout), or f32 (h_fp32)
+    int h_fp32;             // the up epilogue stores h as f32 (orig layout: the h planes read it)
     float *op;              // [P, 1024]
     int *pair_tile;         // [P] tile of each sorted pair
     uint8_t *xq, *hq;       // [NP, P, 512], [NP, P, 1344] e2m1 codes: x, h (x 2^S0 of its tile) as NVFP4 planes
@@ -979,17 +980,32 @@ __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
         const int sbk = __shfl_sync(0xffffffffu, sb_l, blkid);
         uint8_t sc[NP] = {};
         if (live) {
-            const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
-            const float f = d >= -126 ? pow2f(d) : 0.f;
-            const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
-            const uint4 a = src[0], b = src[1];
-            const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
             float w[16];
+            if (p.h_fp32) {   // h as computed: the frame 2^(S0 - HSHIFT) directly
+                const int d = s0 - HSHIFT;
+                const float f = d >= -126 ? pow2f(d) : 0.f;
+                const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.hs) +
+                                                                     (int64_t)pr * INTER + grp * 16);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float2 q = __half22float2(as_h2(u[i]));
-                w[2 * i] = q.x * f;
-                w[2 * i + 1] = q.y * f;
+                for (int i = 0; i < 4; ++i) {
+                    const float4 v = src[i];
+                    w[4 * i] = v.x * f;
+                    w[4 * i + 1] = v.y * f;
+                    w[4 * i + 2] = v.z * f;
+                    w[4 * i + 3] = v.w * f;
+                }
+            } else {          // f16 h of block b carries 2^S_b
+                const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
+                const float f = d >= -126 ? pow2f(d) : 0.f;
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
+                const uint4 a = src[0], b = src[1];
+                const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float2 q = __half22float2(as_h2(u[i]));
+                    w[2 * i] = q.x * f;
+                    w[2 * i + 1] = q.y * f;
+                }
             }
             uint32_t codes[NP][2];
             nvfp4_planes16(w, codes, sc);
@@ -1379,18 +1395,39 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     } else {
         // ------------------------------------------------------------ epilogue (warps 0..3 = TMEM lanes)
         const int m = tid;
+        // The column scales of an item (one per pair: thread c < n owns pair c) are fetched into registers
+        // while the previous item is drained and published to colsc[a] after it, so their global loads
+        // stay off the path between two accumulators.
+        int4 tdn = make_int4(0, 0, 0, 0);
+        float vn = 0.f, s2n = 0.f;
+        int tsn = INT_MAX;
+        auto fetch = [&](int ii) {
+            tdn = p.tiles[ii / MT];
+            s2n = p.s2[(int64_t)tdn.x * 2 + (PH == PH_UP ? 0 : 1)];
+            vn = 0.f;
+            if (tid < tdn.z) vn = PH == PH_UP ? pow2f(-p.pair_exp[tdn.y + tid]) : p.pair_coef[tdn.y + tid];
+            tsn = (PH != PH_UP && lane < MT_UP) ? p.tile_scale[(int64_t)(ii / MT) * MT_UP + lane] : INT_MAX;
+        };
+        auto publish = [&](int buf) {
+            int s0 = tsn;   // down: the tile's smallest block exponent (tile_s0)
+#pragma unroll
+            for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
+            if (tid < tdn.z)
+                colsc[buf * NT + tid] = PH == PH_UP ? vn * s2n : vn * s2n * pow2f(min(HSHIFT - s0, 127));
+        };
+        if (blockIdx.x < nitems) {
+            fetch(blockIdx.x);
+            publish(0);
+        }
         for (int i = blockIdx.x, j = 0; i < nitems; i += gridDim.x, j++) {
             const int tile = i / MT, mt = i % MT;
-            const int4 td = p.tiles[tile];
-            const int e = td.x, n0 = td.y, n = td.z;
+            const int4 td = tdn;
+            const int n0 = td.y, n = td.z;
             const int a = j & 1;
             float *cs = colsc + a * NT;
-            const int s0 = PH != PH_UP ? tile_s0(p, tile, lane) : 0;
-            for (int jj = tid; jj < n; jj += 128) {
-                if (PH == PH_UP) cs[jj] = pow2f(-p.pair_exp[n0 + jj]) * p.s2[(int64_t)e * 2];
-                else cs[jj] = p.pair_coef[n0 + jj] * p.s2[(int64_t)e * 2 + 1] * pow2f(min(HSHIFT - s0, 127));
-            }
-            named_sync(1, 128);
+            named_sync(1, 128);   // this item's column scales are visible; colsc[a ^ 1] is free
+            const bool more = i + (int)gridDim.x < nitems;
+            if (more) fetch(i + gridDim.x);
             const bool acc_ok = warp_wait_bo(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
             tc_fence_after();
             const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
@@ -1421,7 +1458,39 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     }
                 }
             };
-            if (PH == PH_UP) {
+            bool released = false;
+            if (PH == PH_UP && p.h_fp32) {
+                // one pass: h = relu(u)^2 stored as f32 straight from registers (thread m -> neuron m: each
+                // column is one coalesced 512-byte row segment), the block max tracked on the way; the
+                // accumulator is released as soon as its last TMEM read is done
+                float mx = 0.f;
+                float *hrow = reinterpret_cast<float *>(p.hs) + (int64_t)n0 * INTER + mt * BM + m;
+                if (acc_ok) {
+                    for (int c0 = 0; c0 < n; c0 += 32) {
+                        float v[32];
+                        acc32(c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj++) {
+                            if (c0 + jj < n) {
+                                const float u = v[jj] * cs[c0 + jj];
+                                const float hv = u > 0.f ? u * u : 0.f;
+                                mx = fmaxf(mx, hv);
+                                hrow[(int64_t)(c0 + jj) * INTER] = hv;
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[a]);
+                released = true;
+#pragma unroll
+                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                if (lane == 0) red[a * 4 + warp] = mx;
+                named_sync(1, 128);
+                mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
+                if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = mx > 0.f ? prescale_exp(mx, 15) : 127;
+            } else if (PH == PH_UP) {
                 float mx = 0.f;
                 if (acc_ok) {
                     for (int c0 = 0; c0 < n; c0 += 32) {
@@ -1477,9 +1546,12 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                         if (c0 + jj < n) dst[(int64_t)(c0 + jj) * LAT] = v[jj] * cs[c0 + jj];
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
+            if (!released) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[a]);
+            }
+            if (more) publish(a ^ 1);
         }
     }
     tc_fence_before();
@@ -1521,7 +1593,7 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.pair_pos = take(sizeof(int) * (size_t)L.P);
     L.pair_exp = take(sizeof(int) * (size_t)L.P);
     L.tile_scale = take(sizeof(int) * (size_t)L.tiles_cap * MT_UP);
-    L.hs = take((size_t)L.P * INTER * 2);
+    L.hs = take((size_t)L.P * INTER * 4);   // f32 h (orig layout); the T layout uses the first half as f16
     L.op = take((size_t)L.P * LAT * 4);
     L.pair_tile = take(sizeof(int) * (size_t)L.P);
     L.xq = take((size_t)NP * L.P * (LAT / 2));
@@ -1651,6 +1723,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.tile_scale = reinterpret_cast<int *>(ws + L.tile_scale);
     p.xp = nullptr;
     p.hs = reinterpret_cast<__half *>(ws + L.hs);
+    p.h_fp32 = !layout_T;
     p.op = reinterpret_cast<float *>(ws + L.op);
     p.pair_tile = reinterpret_cast<int *>(ws + L.pair_tile);
     p.xq = ws + L.xq;
