@@ -867,18 +867,23 @@ __device__ __forceinline__ void nvfp4_planes16(float (&v)[16], uint32_t (&codes)
         sc[pl] = sb;
         codes[pl][0] = codes[pl][1] = 0u;
         if (!(s > 0.f)) continue;
-        const float inv = 1.f / s;
+        // Any rounding of 1/s only moves a code choice; the residual below subtracts the exact value q * s
+        // that the code and scale encode, so an approximate reciprocal keeps the planes consistent.
+        float inv;
+        asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(s));
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             uint32_t b;
             asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}"
                 : "=r"(b) : "f"(v[2 * i + 1] * inv), "f"(v[2 * i] * inv));
             codes[pl][i >> 2] |= b << (8 * (i & 3));
-            uint32_t h2;
-            asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(b));
-            const float2 q = __half22float2(as_h2(h2));   // (element 2i, element 2i+1)
-            v[2 * i] -= q.x * s;
-            v[2 * i + 1] -= q.y * s;
+            if (pl + 1 < NP) {   // the last plane leaves no residual to carry
+                uint32_t h2;
+                asm("{\n\t.reg .b8 t;\n\tcvt.u8.u32 t, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}" : "=r"(h2) : "r"(b));
+                const float2 q = __half22float2(as_h2(h2));   // (element 2i, element 2i+1)
+                v[2 * i] -= q.x * s;
+                v[2 * i + 1] -= q.y * s;
+            }
         }
     }
 }
