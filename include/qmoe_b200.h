@@ -135,7 +135,8 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
  * the moe_pairs arithmetic (qmoe_ns.py:79-133) and the per-expert fp32 path (nem_super.py:342-346) as
  * one expert-grouped GEMM on the tensor cores: block-scaled NVFP4 tcgen05 MMA on the stored weights with the
  * activations as three NVFP4 residual planes (orig layout; the T layout's down half decodes dnT_w exactly to
- * f16), fp32 accumulation, h kept as f16 with power-of-two block scales. Expert e's block is at
+ * f16), fp32 accumulation; h is kept as f32 (orig layout) or as f16 with power-of-two block scales (T layout).
+ * Expert e's block is at
  * store + e * block_stride (block_stride >= BLOCK, multiple of 16); layout_T selects the T layout of the
  * down half (else the orig layout). s2 [n_experts, 2] f32; x [T,1024] in x_dtype (bf16 is converted
  * exactly); out [T,1024] f32. Id -1 means "no expert" (the pair is skipped; expert-parallel blocks use it for
