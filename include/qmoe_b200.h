@@ -143,7 +143,7 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
  * experts on other ranks); any other id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
  * and makes that token's output NaN. 1 <= T <= 65536, 1 <= topk <= 32, 1 <= n_experts <= 1024.
  * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts) bytes, 256-byte aligned) holds the
- * sorted pairs, their activation planes and f16 h rows; its status word must start at zero. */
+ * sorted pairs, their activation planes and the h rows; its status word must start at zero. */
 size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts);
 int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
                          const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
