@@ -26,6 +26,10 @@
 #include "common.cuh"
 #include "host.h"
 
+#ifndef QMOE_PF_T_F16
+#define QMOE_PF_T_F16 0   // T-layout prompts: 0 = convert the down halves and run the block-scaled GEMM
+#endif
+
 namespace qmoe {
 namespace pf {
 
@@ -56,6 +60,8 @@ constexpr int TMEM_COLS = 2 * NT;       // two accumulators: the epilogue of one
 constexpr int ROW512_DNT = (int)(O_DW / 512);     // 3024: dnT_w
 constexpr int ROW1024_DNT_S = (int)(O_DS / 1024); // 2856: dnT_s
 constexpr int ROW1344_DW = (int)(O_DW / 1344);    // 1152: dn_w
+constexpr int64_t DC_W = (int64_t)LAT * KB_DN;      // 1,376,256 B: orig-layout down codes
+constexpr int64_t DC_STRIDE = DC_W + (int64_t)LAT * G_DN;   // + 172,032 B of scales: one converted down half
 static_assert(O_DW % 512 == 0 && O_DS % 1024 == 0 && O_DW % 1344 == 0 && BLOCK % 1344 == 0, "block regions on view rows");
 
 // Shared memory carve-up, from a 1024-byte aligned base (the 128B swizzle repeats every 1024 bytes).
@@ -104,7 +110,13 @@ struct Params {
     int *tile_scale;        // [tiles_cap, 21]
     __half *xp;             // [P, 1024]
     __half *hs;             // [P, 2688] f16 x 2^S_b per 128-row block (T layout), or f32 (h_fp32)
-    int h_fp32;             // the up epilogue stores h as f32 (orig layout: the h planes read it)
+    int h_fp32;             // the up epilogue stores h as f32 (the h planes read it)
+    const uint8_t *dn_w;    // down codes [1024 rows][1344 B] of expert e at dn_w + e * dn_bstride (row dn_row0)
+    const uint8_t *dn_sc;   // down scales [1024][168] of expert e at dn_sc + e * dn_bstride
+    int64_t dn_bstride;
+    int dn_row0;
+    uint8_t *dconv;         // T layout: the used experts' down halves converted to the orig layout
+                            // [ne][1376256 B codes | 172032 B scales]
     float *op;              // [P, 1024]
     int *pair_tile;         // [P] tile of each sorted pair
     uint8_t *xq, *hq;       // [NP, P, 512], [NP, P, 1344] e2m1 codes: x, h (x 2^S0 of its tile) as NVFP4 planes
@@ -1167,7 +1179,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     mbar_expect_tx(&full[s], (uint32_t)(nh * BS_A));
                     for (int hh = 0; hh < nh; hh++)
                         tma_load_3d(sm + s * BS_STAGE + hh * BS_A, &tm_w, (k0 + hh) * (BS_BK / 2),
-                                    (PH == PH_UP ? 0 : ROW1344_DW) + mt * BM, e, &full[s]);
+                                    (PH == PH_UP ? 0 : p.dn_row0) + mt * BM, e, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -1219,13 +1231,14 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         // of two slabs, the next item's copy in flight while this item is built. Stage kt takes bytes
         // 8kt .. 8kt+7 of each row: atom kk, lane L = rows L, L+32, L+64, L+96, 4 bytes each.
         uint8_t *slab = sm + Plan::OFF_SLAB;
-        const uint8_t *wsc0 = p.store + (PH == PH_UP ? O_US : O_DS);
+        const uint8_t *wsc0 = PH == PH_UP ? p.store + O_US : p.dn_sc;
+        const int64_t wstride = PH == PH_UP ? p.bstride : p.dn_bstride;
         uint32_t issued[2] = {0, 0}, done[2] = {0, 0};
         if (blockIdx.x < nitems) {
             if (lane == 0) {
                 const int i = blockIdx.x;
                 mbar_expect_tx(&slab_full[0], Plan::SLAB);
-                bulk_g2s_nohint(slab, wsc0 + (int64_t)p.tiles[i / MT].x * p.bstride + (int64_t)(i % MT) * Plan::SLAB,
+                bulk_g2s_nohint(slab, wsc0 + (int64_t)p.tiles[i / MT].x * wstride + (int64_t)(i % MT) * Plan::SLAB,
                                 Plan::SLAB, &slab_full[0]);
             }
             issued[0] = 1;
@@ -1241,7 +1254,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     fence_async_smem();
                     mbar_expect_tx(&slab_full[b ^ 1], Plan::SLAB);
                     bulk_g2s_nohint(slab + (b ^ 1) * Plan::SLAB,
-                                    wsc0 + (int64_t)p.tiles[inext / MT].x * p.bstride + (int64_t)(inext % MT) * Plan::SLAB,
+                                    wsc0 + (int64_t)p.tiles[inext / MT].x * wstride + (int64_t)(inext % MT) * Plan::SLAB,
                                     Plan::SLAB, &slab_full[b ^ 1]);
                 }
                 issued[b ^ 1]++;
@@ -1567,10 +1580,92 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------------------------------------ T -> orig down
+// A T-layout store keeps dnT_w [2688 neurons][512 B] (neuron-major: the output rows of a neuron together),
+// which FP4 operands of the tensor core cannot take (they must be K-major). For a prompt the down halves of the
+// experts the prompt uses are converted once into dconv, [1024 rows][1344 B] codes then [1024][168] scales
+// per expert - the orig layout, as from_T_fast does for the reference's prompt path (nem_super.py:324-328) -
+// and the block-scaled down GEMM reads them there. Experts with no pair are skipped.
+constexpr int DCV_R = 64, DCV_C = 128;   // scales: 128 rows per CTA; codes: 64 neurons x 256 rows per CTA
+
+// 8 x 8 nibble transpose in registers: w[i] holds nibbles (i, 0..7) at bits 4j; afterwards w[j] holds
+// nibbles (0..7, j) at bits 4i. Three rounds of masked swaps (16-bit halves, bytes, nibbles).
+__device__ __forceinline__ void nibble_transpose8(uint32_t (&w)[8]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t a = w[i], b = w[i + 4];
+        w[i] = (a & 0x0000FFFFu) | (b << 16);
+        w[i + 4] = (a >> 16) | (b & 0xFFFF0000u);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i += (i & 1) ? 3 : 1) {   // i = 0, 1, 4, 5
+        const uint32_t a = w[i], b = w[i + 2];
+        w[i] = (a & 0x00FF00FFu) | ((b & 0x00FF00FFu) << 8);
+        w[i + 2] = ((a >> 8) & 0x00FF00FFu) | (b & 0xFF00FF00u);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const uint32_t a = w[i], b = w[i + 1];
+        w[i] = (a & 0x0F0F0F0Fu) | ((b & 0x0F0F0F0Fu) << 4);
+        w[i + 1] = ((a >> 4) & 0x0F0F0F0Fu) | (b & 0xF0F0F0F0u);
+    }
+}
+
+// dnT_w [2688 neurons][512 B] -> dn_w [1024 rows][1344 B]: a CTA stages 64 neurons x 256 output rows (128 B
+// per neuron) in shared memory; thread (a, b) transposes the 8 x 8 nibble block of neurons 8a.. and rows 8b..
+// and writes 4 bytes to each of its 8 output rows (8 consecutive lanes fill one 32-byte sector).
+__global__ void __launch_bounds__(256) pf_dnT_codes_kernel(const Params p) {
+    __shared__ uint32_t tile[DCV_R][33];
+    const int e = blockIdx.z;
+    if (p.cnt[e] == 0) return;
+    const int n0 = blockIdx.x * DCV_R, r0 = blockIdx.y * 256;
+    const uint8_t *A = p.store + (int64_t)e * p.bstride + O_DW;   // [2688][512 B]
+    uint8_t *B = p.dconv + (int64_t)e * DC_STRIDE;                 // [1024][1344 B]
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int idx = tid + 256 * k, row = idx >> 3, part = idx & 7;
+        const uint4 v = *reinterpret_cast<const uint4 *>(A + (int64_t)(n0 + row) * (LAT / 2) + r0 / 2 + 16 * part);
+        tile[row][4 * part] = v.x, tile[row][4 * part + 1] = v.y, tile[row][4 * part + 2] = v.z, tile[row][4 * part + 3] = v.w;
+    }
+    __syncthreads();
+    const int a = tid & 7, b = tid >> 3;
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = tile[8 * a + i][b];
+    nibble_transpose8(w);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<uint32_t *>(B + (int64_t)(r0 + 8 * b + j) * KB_DN + n0 / 2 + 4 * a) = w[j];
+}
+
+// dnT_s [168 groups][1024 rows] -> [1024 rows][168 groups] for 128 rows per CTA.
+__global__ void __launch_bounds__(256) pf_dnT_scales_kernel(const Params p) {
+    __shared__ __align__(16) uint8_t s[G_DN][DCV_C + 4];
+    const int e = blockIdx.y;
+    if (p.cnt[e] == 0) return;
+    const int r0 = blockIdx.x * DCV_C;
+    const uint8_t *A = p.store + (int64_t)e * p.bstride + O_DS;   // [168][1024]
+    uint8_t *B = p.dconv + (int64_t)e * DC_STRIDE + DC_W;          // [1024][168]
+    for (int i = threadIdx.x; i < G_DN * (DCV_C / 16); i += blockDim.x) {
+        const int g = i >> 3, part = i & 7;
+        const uint4 v = *reinterpret_cast<const uint4 *>(A + (int64_t)g * LAT + r0 + 16 * part);
+        uint32_t *d = reinterpret_cast<uint32_t *>(&s[g][16 * part]);
+        d[0] = v.x, d[1] = v.y, d[2] = v.z, d[3] = v.w;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < DCV_C * (G_DN / 4); i += blockDim.x) {   // 4 scale bytes per store
+        const int rr = i / (G_DN / 4), g4 = (i - rr * (G_DN / 4)) * 4;
+        const uint32_t v = (uint32_t)s[g4][rr] | ((uint32_t)s[g4 + 1][rr] << 8) | ((uint32_t)s[g4 + 2][rr] << 16) |
+                           ((uint32_t)s[g4 + 3][rr] << 24);
+        *reinterpret_cast<uint32_t *>(B + (int64_t)(r0 + rr) * G_DN + g4) = v;
+    }
+}
+
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
     size_t status, tile_count, cnt, eoff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
-        hs, op, pair_tile, xq, hq, sfbx, sfbh, total;
+        hs, op, pair_tile, xq, hq, sfbx, sfbh, dconv, total;
     int P, nchunks, tiles_cap;
 };
 
@@ -1604,6 +1699,7 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.xq = take((size_t)NP * L.P * (LAT / 2));
     L.hq = take((size_t)NP * L.P * KB_DN);
     L.sfbx = take((size_t)L.tiles_cap * KS_UP * NP * BS_ATOM);
+    L.dconv = take((size_t)ne * DC_STRIDE);   // T layout: converted down halves
     L.sfbh = take((size_t)L.tiles_cap * KS_DN * NP * BS_ATOM);
     L.total = o;
     return L;
@@ -1642,10 +1738,10 @@ inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int
 // The store as a u8 tensor [ne][BLOCK / pitch][pitch] (expert stride bstride), for TMA boxes of
 // {box_x bytes, box_y rows} out of one block region.
 inline bool make_store_map(CUtensorMap *m, const void *store, int64_t bstride, int ne, int pitch, int box_x,
-                           int box_y, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE) {
+                           int box_y, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE, int64_t span = BLOCK) {
     EncodeTiledFn fn = encode_tiled();
     if (!fn) return false;
-    const cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)(BLOCK / pitch), (cuuint64_t)ne};
+    const cuuint64_t dims[3] = {(cuuint64_t)pitch, (cuuint64_t)(span / pitch), (cuuint64_t)ne};
     const cuuint64_t strides[2] = {(cuuint64_t)pitch, (cuuint64_t)bstride};
     const cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)box_y, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
@@ -1728,7 +1824,19 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.tile_scale = reinterpret_cast<int *>(ws + L.tile_scale);
     p.xp = nullptr;
     p.hs = reinterpret_cast<__half *>(ws + L.hs);
-    p.h_fp32 = !layout_T;
+    p.h_fp32 = QMOE_PF_T_F16 ? !layout_T : 1;
+    p.dconv = ws + L.dconv;
+    if (layout_T && !QMOE_PF_T_F16) {   // the down GEMM reads the converted halves
+        p.dn_w = p.dconv;
+        p.dn_sc = p.dconv + DC_W;
+        p.dn_bstride = DC_STRIDE;
+        p.dn_row0 = 0;
+    } else {
+        p.dn_w = store;
+        p.dn_sc = store + O_DS;
+        p.dn_bstride = block_stride;
+        p.dn_row0 = ROW1344_DW;
+    }
     p.op = reinterpret_cast<float *>(ws + L.op);
     p.pair_tile = reinterpret_cast<int *>(ws + L.pair_tile);
     p.xq = ws + L.xq;
@@ -1739,24 +1847,28 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     // up: block-scaled NVFP4 (weights as stored, x as NVFP4 planes); down: block-scaled on the orig layout,
     // or the exact-f16 kernel on the T layout (FP4 operands of the tensor core must be K-major)
     const int hts[4] = {16, 32, 64, 128};
+    const bool f16_down = layout_T && QMOE_PF_T_F16;
     CUtensorMap xm[4], hm[4], bh[4], wu, wdo, wdt, sdt;
     for (int k = 0; k < 4; k++) {
         if (!make_plane_map(&xm[k], p.xq, L.P, LAT / 2, hts[k])) return QMOE_ERR_LAUNCH;
-        if (layout_T ? !make_map(&bh[k], p.hs, L.P, INTER, hts[k]) : !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
+        if (f16_down ? !make_map(&bh[k], p.hs, L.P, INTER, hts[k]) : !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
             return QMOE_ERR_LAUNCH;
     }
     if (!make_store_map(&wu, store, block_stride, n_experts, KB_UP, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;
-    if (layout_T) {
+    if (f16_down) {
         if (!make_store_map(&wdt, store, block_stride, n_experts, 512, BM / 2, RK) ||
             !make_store_map(&sdt, store, block_stride, n_experts, 1024, BM, G_DN))
             return QMOE_ERR_LAUNCH;
-    } else if (!make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    } else if (layout_T ? !make_store_map(&wdo, p.dconv, DC_STRIDE, n_experts, KB_DN, BS_BK / 2, BM,
+                                          CU_TENSOR_MAP_SWIZZLE_64B, DC_STRIDE)
+                        : !make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM,
+                                          CU_TENSOR_MAP_SWIZZLE_64B)) {
         return QMOE_ERR_LAUNCH;
     }
     auto up = pfb_gemm_kernel<PH_UP>;
     if (!ensure_smem(up, BsPlan<PH_UP>::SMEM, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
-    if (layout_T ? !ensure_smem(pf_gemm_kernel<PH_DN_T>, SMEM_BYTES, dev, g_smem_dn_t)
+    if (f16_down ? !ensure_smem(pf_gemm_kernel<PH_DN_T>, SMEM_BYTES, dev, g_smem_dn_t)
                  : !ensure_smem(pfb_gemm_kernel<PH_DN_O>, BsPlan<PH_DN_O>::SMEM, dev, g_smem_dn_o))
         return QMOE_ERR_LAUNCH;
 
@@ -1765,8 +1877,12 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
     pf_xplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
+    if (layout_T && !f16_down) {
+        pf_dnT_codes_kernel<<<dim3(INTER / DCV_R, LAT / 256, n_experts), 256, 0, st>>>(p);
+        pf_dnT_scales_kernel<<<dim3(LAT / DCV_C, n_experts), 256, 0, st>>>(p);
+    }
     up<<<di->sms, BS_THREADS, BsPlan<PH_UP>::SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
-    if (layout_T) {
+    if (f16_down) {
         pf_gemm_kernel<PH_DN_T><<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wdt, wdt, sdt);
     } else {
         pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
