@@ -134,16 +134,17 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
  *   out[t] = sum_k (in k order) weights[t,k] * s2[e,1] * D_e relu(s2[e,0] * U_e x[t])^2,  e = ids[t,k],
  * the moe_pairs arithmetic (qmoe_ns.py:79-133) and the per-expert fp32 path (nem_super.py:342-346) as
  * one expert-grouped GEMM on the tensor cores: block-scaled NVFP4 tcgen05 MMA on the stored weights with the
- * activations as three NVFP4 residual planes (orig layout; the T layout's down half decodes dnT_w exactly to
- * f16), fp32 accumulation; h is kept as f32 (orig layout) or as f16 with power-of-two block scales (T layout).
- * Expert e's block is at
+ * activations as three NVFP4 residual planes, fp32 accumulation, h kept as f32. With a T-layout store the down
+ * halves of the experts the prompt uses are first converted to the orig layout inside the workspace (as the
+ * reference's prompt path does with from_T_fast); both layouts give identical results. Expert e's block is at
  * store + e * block_stride (block_stride >= BLOCK, multiple of 16); layout_T selects the T layout of the
  * down half (else the orig layout). s2 [n_experts, 2] f32; x [T,1024] in x_dtype (bf16 is converted
  * exactly); out [T,1024] f32. Id -1 means "no expert" (the pair is skipped; expert-parallel blocks use it for
  * experts on other ranks); any other id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
  * and makes that token's output NaN. 1 <= T <= 65536, 1 <= topk <= 32, 1 <= n_experts <= 1024.
  * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts) bytes, 256-byte aligned) holds the
- * sorted pairs, their activation planes and the h rows; its status word must start at zero. */
+ * sorted pairs, their activation planes, the h rows and room for n_experts converted down halves (1.55 MB
+ * each, used for a T-layout store); its status word must start at zero. */
 size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts);
 int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
                          const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,

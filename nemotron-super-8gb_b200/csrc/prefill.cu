@@ -1,5 +1,5 @@
 // Prefill: the routed-expert forward for T tokens at once, as an expert-grouped GEMM on the 5th-generation
-// tensor cores (tcgen05.mma, accumulators in tensor memory).
+// tensor cores (block-scaled NVFP4 tcgen05.mma, accumulators in tensor memory).
 //
 // Replaces the reference's prompt path (nem_super.py:295-348): the pair path moe_pairs
 // (qmoe_ns.py:79-133, used for T <= 64) and the per-expert CPU/fp32 path (block_deq + two F.linear per
@@ -7,84 +7,39 @@
 //
 // Pipeline (all on the caller's stream, nothing allocated):
 //   1. pf_hist / pf_scan / pf_place: a deterministic counting sort of the T*topk (token, k) pairs by
-//      expert. Pairs of one expert are contiguous and ordered by token; tiles of <= 256 pairs per expert.
-//   2. pf_gather: Xp[p] = f16(x[token(p)] * 2^E), with E the per-pair power of two that puts the token's
-//      amax in [2^14, 2^15): the bf16 -> f16 conversion is then exact.
-//   3. pf_gemm<UP>: per (tile, 128 up rows): D[128 rows, N pairs] = W_up (f16, decoded exactly from NVFP4
-//      by producer warps into shared memory) x Xp^T (TMA, 128B swizzle); epilogue u = D * 2^-E * s2u,
-//      h = relu(u)^2, written as f16 with one power-of-two scale per (tile, 128-row block) so the block's
-//      amax lands in [2^14, 2^15).
-//   4. pf_gemm<DOWN>: per (tile, 128 output rows): D = (W_down * 2^(S0 - S_block)) x Hs^T over K = 2688,
-//      the per-block h scales folded into the decoded weights (exact powers of two); epilogue
-//      y = D * 2^-S0 * s2d * coef -> Op[pair] fp32.
-//   5. pf_combine: out[t] = sum_k Op[pos(t, k)] in k order (deterministic, as nem_super.py:309-347).
-//
-// Every product e2m1 * e4m3 (at most 5 significant bits, magnitude in [2^-10, 2688]) is exact in f16,
-// so the only roundings are the fp32 accumulation and the f16 storage of h (relative 2^-12).
+//      expert. Pairs of one expert are contiguous and ordered by token; tiles of <= 128 pairs per expert.
+//   2. pf_xplanes: x[token] * 2^E as three NVFP4 residual planes, their scales as tcgen05 scale atoms.
+//   3. (T layout only) pf_dnT_codes / pf_dnT_scales: the used experts' down halves converted to the orig
+//      (K-major) layout in the workspace.
+//   4. pfb_gemm<UP>: per (tile, 128 up rows): D = W_up (NVFP4 as stored) x planes^T, block-scaled MMA;
+//      epilogue u = D * 2^-E * s2u, h = relu(u)^2 stored as f32.
+//   5. pf_hplanes: h in its tile's frame as three NVFP4 planes.
+//   6. pfb_gemm<DOWN>: per (tile, 128 output rows), K = 2688; epilogue y = D * 2^(4 - S0) * s2d * coef.
+//   7. pf_combine: out[t] = sum_k Op[pos(t, k)] in k order (deterministic, as nem_super.py:309-347).
 #include <cuda.h>
 
 #include "common.cuh"
 #include "host.h"
-
-#ifndef QMOE_PF_T_F16
-#define QMOE_PF_T_F16 0   // T-layout prompts: 0 = convert the down halves and run the block-scaled GEMM
-#endif
 
 namespace qmoe {
 namespace pf {
 
 constexpr int NT = 128;                 // pairs per tile = largest MMA N used
 constexpr int BM = 128;                 // MMA M (rows of the weight tile)
-constexpr int BK = 64;                  // K per A/B stage (4 MMAs of K = 16)
-constexpr int RK = 128;                 // K per raw-weight stage: one 8 KB TMA box
-constexpr int KPR = RK / BK;            // A stages filled from one raw stage
-constexpr int SA = 4, SB = 4, SR = 6;   // ring depths: A (decoded weights), B (activations), raw weights
-constexpr int A_BYTES = BM * BK * 2;    // 16 KB f16
-constexpr int B_BYTES = NT * BK * 2;    // 16 KB f16
-constexpr int RAW_BYTES = BM * RK / 2;  // 8 KB of e2m1 codes
-constexpr int SLAB_BYTES = 128 * 168;   // e4m3 scales of one item (largest: down, 168 groups x 128 rows)
-constexpr int STG_COLS = 16;            // epilogue staging: 16 pairs x 128 rows of f16
-constexpr int NDEC = 256;               // decoder threads (warps 4..11)
-constexpr int W_RAW = 12, W_B = 13, W_MMA = 14;
-constexpr int THREADS = 15 * 32;        // warps 0..3 epilogue, 4..11 decoders, 12 raw TMA, 13 B TMA, 14 MMA
 constexpr int MT_UP = INTER / BM;       // 21
 constexpr int MT_DN = LAT / BM;         // 8
-constexpr int NKT_UP = LAT / BK;        // 16
-constexpr int NKT_DN = INTER / BK;      // 42
 constexpr int CHUNK_T = 64;             // tokens per routing chunk
 constexpr int MAX_NE = 1024;
 constexpr int MAX_TOPK = 32;
 constexpr int MAX_T = 65536;
-constexpr int TMEM_COLS = 2 * NT;       // two accumulators: the epilogue of one item overlaps the next
 // Row offsets of the block regions in the TMA views of the store (row pitch 512, 1024, 1344 bytes).
-constexpr int ROW512_DNT = (int)(O_DW / 512);     // 3024: dnT_w
-constexpr int ROW1024_DNT_S = (int)(O_DS / 1024); // 2856: dnT_s
 constexpr int ROW1344_DW = (int)(O_DW / 1344);    // 1152: dn_w
 constexpr int64_t DC_W = (int64_t)LAT * KB_DN;      // 1,376,256 B: orig-layout down codes
 constexpr int64_t DC_STRIDE = DC_W + (int64_t)LAT * G_DN;   // + 172,032 B of scales: one converted down half
-static_assert(O_DW % 512 == 0 && O_DS % 1024 == 0 && O_DW % 1344 == 0 && BLOCK % 1344 == 0, "block regions on view rows");
+static_assert(O_DW % 1344 == 0 && BLOCK % 1344 == 0, "dn_w on 1344-byte view rows");
 
 // Shared memory carve-up, from a 1024-byte aligned base (the 128B swizzle repeats every 1024 bytes).
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + SA * A_BYTES;
-constexpr int OFF_RAW = OFF_B + SB * B_BYTES;
-constexpr int OFF_SLAB = OFF_RAW + SR * RAW_BYTES;         // two item scale buffers
-constexpr int OFF_STG = OFF_SLAB + 2 * SLAB_BYTES;
-constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;     // 2 x NT f32 per-column epilogue factors
-constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;            // 2 x 4 f32 block-amax partials
-constexpr int OFF_BAR = OFF_RED + 32;
-constexpr int NBAR = 2 * SA + 2 * SB + 2 * SR + 8;
-constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
-constexpr int OFF_ABORT = OFF_TMEM + 16;
-constexpr int SMEM_USED = OFF_ABORT + 16;
-constexpr int SMEM_BYTES = SMEM_USED + 1024;               // + alignment slack
-static_assert(SMEM_BYTES <= 232448, "fits the 227 KB opt-in");
-static_assert(OFF_RAW % 1024 == 0 && OFF_B % 1024 == 0 && OFF_SLAB % 16 == 0, "TMA destinations");
-static_assert(LAT % RK == 0 && INTER % RK == 0 && INTER % BM == 0 && LAT % BM == 0, "tiling");
-constexpr int UNITS = BM * RK / 2 / 16 / NDEC;   // 16-byte raw chunks per decoder thread and stage
-constexpr int PPR = RK / 32;                     // 16-byte parts per K-major row of a raw stage
-
-enum { PH_UP = 0, PH_DN_T = 1, PH_DN_O = 2 };
+enum { PH_UP = 0, PH_DN_O = 2 };
 
 struct Params {
     const uint8_t *store;   // expert e's block at store + e * bstride
@@ -108,9 +63,7 @@ struct Params {
     int *pair_pos;          // [T * topk] sorted position of (t, k), -1 if the id was invalid
     int *pair_exp;          // [P]
     int *tile_scale;        // [tiles_cap, 21]
-    __half *xp;             // [P, 1024]
-    __half *hs;             // [P, 2688] f16 x 2^S_b per 128-row block (T layout), or f32 (h_fp32)
-    int h_fp32;             // the up epilogue stores h as f32 (the h planes read it)
+    float *hs;              // [P, 2688] h = relu(u)^2 of every pair, f32 (the h planes read it)
     const uint8_t *dn_w;    // down codes [1024 rows][1344 B] of expert e at dn_w + e * dn_bstride (row dn_row0)
     const uint8_t *dn_sc;   // down scales [1024][168] of expert e at dn_sc + e * dn_bstride
     int64_t dn_bstride;
@@ -284,20 +237,6 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint3
            ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
-// Instruction descriptor of kind::f16: f32 accumulator, A and B f16, B K-major, M = 128, N = n.
-__device__ __forceinline__ uint32_t instr_desc_f16(int n, bool a_mn_major) {
-    return (1u << 4) | ((a_mn_major ? 1u : 0u) << 15) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
 // Arrives on `bar` once every tcgen05.mma this thread issued before has completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -319,28 +258,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// 2-D tiled TMA load of one box into this CTA's shared memory, completing on `bar`.
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-// 2^d as f16x2 for d <= 0 (exact while 2^d >= 2^-24, zero below).
-__device__ __forceinline__ uint32_t pow2_h2(int d) {
-    uint32_t h;
-    if (d >= -14) h = (uint32_t)(15 + d) << 10;
-    else if (d >= -24) h = 1u << (d + 24);
-    else h = 0u;
-    return h | (h << 16);
 }
 
 // 3-D tiled TMA load (box {x, y, 1}) into this CTA's shared memory, completing on `bar`.
@@ -371,34 +288,6 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
         : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
-
-// Bounded wait by lane 0 of a warp, result broadcast to the warp. On timeout: record it, raise the CTA's
-// abort flag and return false; once the flag is up every wait returns false at once, so each role leaves
-// (or, for the epilogue, runs out) its item loop without waiting again.
-__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, int lane, volatile int *abort_flag,
-                                          int *status) {
-    bool ok = true;
-    if (lane == 0) {
-        ok = !*abort_flag && mbar_wait(bar, parity);
-        if (!ok) {
-            set_error(status, DEV_ERR_TIMEOUT);
-            *abort_flag = 1;
-        }
-    }
-    return __shfl_sync(0xffffffffu, ok, 0);
-}
 
 __device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
     const bool ok = !*abort_flag && mbar_wait(bar, parity);
@@ -407,399 +296,6 @@ __device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volati
         *abort_flag = 1;
     }
     return ok;
-}
-
-// Decodes one 16-byte raw chunk (32 e2m1 codes) of a K-major row into four 8-code chunks of the A tile:
-// chunk c of row m at (m/8)*1024 + c*128 + (m%8)*16 (no swizzle; LBO 128 along k, SBO 1024 along m).
-// sc: the two e4m3 scales of the 32 codes as f16x2 (times the down factor).
-__device__ __forceinline__ void put_kmajor(uint32_t a_tile, int m, int c0, uint4 raw, __half2 sc) {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    const __half2 sa = __low2half2(sc), sb = __high2half2(sc);
-    const uint32_t row = a_tile + (m >> 3) * 1024 + (m & 7) * 16;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        uint32_t o[4];
-        e2m1x8_f16x2(w[i], o);
-        const __half2 s = i < 2 ? sa : sb;
-        st_shared_v4(row + (c0 + i) * 128, h2_as_u(__hmul2(as_h2(o[0]), s)), h2_as_u(__hmul2(as_h2(o[1]), s)),
-                     h2_as_u(__hmul2(as_h2(o[2]), s)), h2_as_u(__hmul2(as_h2(o[3]), s)));
-    }
-}
-
-// Decodes one 16-byte raw chunk of the T layout (32 output rows 32q..32q+31 at input neuron kl) into the
-// MN-major A tile: rows 8j..8j+7 at k = kl sit at j*1024 + (kl/8)*128 + (kl%8)*16 (LBO 128 along k,
-// SBO 1024 along m). srow: the 32 e4m3 scales of those rows; f: the down factor.
-__device__ __forceinline__ void put_mnmajor(uint32_t a_tile, int kl, int q, uint4 raw, const uint8_t *srow, __half2 f) {
-    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-    const uint32_t kaddr = a_tile + (kl >> 3) * 128 + (kl & 7) * 16;
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        const uint2 s8 = *reinterpret_cast<const uint2 *>(srow + i * 8);
-        uint32_t s[4];
-        e4m3x4_f16x2(s8.x, s[0], s[1]);
-        e4m3x4_f16x2(s8.y, s[2], s[3]);
-        uint32_t o[4];
-        e2m1x8_f16x2(w[i], o);
-        st_shared_v4(kaddr + (q * 4 + i) * 1024, h2_as_u(__hmul2(as_h2(o[0]), __hmul2(as_h2(s[0]), f))),
-                     h2_as_u(__hmul2(as_h2(o[1]), __hmul2(as_h2(s[1]), f))),
-                     h2_as_u(__hmul2(as_h2(o[2]), __hmul2(as_h2(s[2]), f))),
-                     h2_as_u(__hmul2(as_h2(o[3]), __hmul2(as_h2(s[3]), f))));
-    }
-}
-
-// Smallest h-block scale exponent of a tile (the block with the largest amax) over its 21 up blocks,
-// reduced across one warp.
-__device__ __forceinline__ int tile_s0(const Params &p, int tile, int lane) {
-    int m = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
-    return m;
-}
-
-// The grouped GEMM, persistent: one CTA per SM walks the items (tile, 128-row block) i = blockIdx.x,
-// blockIdx.x + gridDim.x, ...; consecutive items share a tile (its activations stay in L2).
-// Roles: warp 12 streams each item's scales (one copy) and its raw weights (16 KB TMA boxes of 256 k) into
-// a 3-deep ring; warps 4..11 decode them into f16 A stages (64 k each); warp 13 loads the activation (B)
-// stages with TMA (one box of 16..128 pair rows per k-stage); warp 14 issues tcgen05.mma into one of two
-// TMEM accumulators while warps 0..3 drain the other one (epilogue).
-template <int PH>
-__global__ void __launch_bounds__(THREADS, 1)
-    pf_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_b16, const __grid_constant__ CUtensorMap tm_b32,
-                   const __grid_constant__ CUtensorMap tm_b64, const __grid_constant__ CUtensorMap tm_b128,
-                   const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_w2,
-                   const __grid_constant__ CUtensorMap tm_s) {
-    constexpr int MT = PH == PH_UP ? MT_UP : MT_DN;
-    constexpr int NKT = PH == PH_UP ? NKT_UP : NKT_DN;
-    constexpr int NKR = (NKT + KPR - 1) / KPR;
-    const int nitems = *p.tile_count * MT;
-
-    extern __shared__ uint8_t smem_raw[];
-    const uint32_t raw_base = smem_u32(smem_raw);
-    uint8_t *sm = smem_raw + (((raw_base + 1023u) & ~1023u) - raw_base);
-    const uint32_t sbase = smem_u32(sm);
-    float *colsc = reinterpret_cast<float *>(sm + OFF_COLSC);
-    float *red = reinterpret_cast<float *>(sm + OFF_RED);
-    __half *stg = reinterpret_cast<__half *>(sm + OFF_STG);
-    uint64_t *a_full = reinterpret_cast<uint64_t *>(sm + OFF_BAR);
-    uint64_t *a_empty = a_full + SA;
-    uint64_t *b_full = a_empty + SA;
-    uint64_t *b_empty = b_full + SB;
-    uint64_t *raw_full = b_empty + SB;
-    uint64_t *raw_empty = raw_full + SR;
-    uint64_t *acc_full = raw_empty + SR;
-    uint64_t *acc_empty = acc_full + 2;
-    uint64_t *slab_full = acc_empty + 2;
-    uint64_t *slab_empty = slab_full + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + OFF_TMEM);
-    volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + OFF_ABORT);
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    if (tid == 0) {
-        for (int s = 0; s < SA; s++) {
-            mbar_init(&a_full[s], NDEC / 32);
-            mbar_init(&a_empty[s], 1);
-        }
-        for (int s = 0; s < SB; s++) {
-            mbar_init(&b_full[s], 1);
-            mbar_init(&b_empty[s], 1);
-        }
-        for (int r = 0; r < SR; r++) {
-            mbar_init(&raw_full[r], 1);
-            mbar_init(&raw_empty[r], NDEC / 32);
-        }
-        for (int a = 0; a < 2; a++) {
-            mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 4);
-            mbar_init(&slab_full[a], 1);
-            mbar_init(&slab_empty[a], NDEC / 32);
-        }
-        *abort_flag = 0;
-        fence_mbar_init();
-    }
-    if (warp == W_MMA) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == W_RAW) {
-        // ------------------------------------------------------------ scales (per item) + raw weights -> rings
-        if (lane == 0) {
-            uint32_t q = 0;
-            int e_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].x : 0;   // one item ahead
-            for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
-                const int mt = i % MT;
-                const int e = e_next;
-                if (i + (int)gridDim.x < nitems) e_next = p.tiles[(i + gridDim.x) / MT].x;
-                const uint8_t *blk = p.store + (int64_t)e * p.bstride;
-                const int sb = j & 1;
-                if (!lane_wait(&slab_empty[sb], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-                uint8_t *slab = sm + OFF_SLAB + sb * SLAB_BYTES;
-                if (PH == PH_UP) {
-                    mbar_expect_tx(&slab_full[sb], BM * G_UP);
-                    bulk_g2s(slab, blk + O_US + (int64_t)mt * BM * G_UP, BM * G_UP, &slab_full[sb], policy_evict_first());
-                } else if (PH == PH_DN_O) {
-                    mbar_expect_tx(&slab_full[sb], BM * G_DN);
-                    bulk_g2s(slab, blk + O_DS + (int64_t)mt * BM * G_DN, BM * G_DN, &slab_full[sb], policy_evict_first());
-                } else {
-                    mbar_expect_tx(&slab_full[sb], BM * G_DN);
-                    tma_load_3d(slab, &tm_s, mt * BM, ROW1024_DNT_S, e, &slab_full[sb]);
-                }
-                bool ok = true;
-                for (int kr = 0; kr < NKR; kr++, q++) {
-                    const int r = q % SR;
-                    if (!lane_wait(&raw_empty[r], ((q / SR) & 1) ^ 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *dst = sm + OFF_RAW + r * RAW_BYTES;
-                    if (PH == PH_UP) {
-                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
-                        tma_load_3d(dst, &tm_w, kr * (RK / 2), mt * BM, e, &raw_full[r]);
-                    } else if (PH == PH_DN_T) {
-                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
-                        tma_load_3d(dst, &tm_w, mt * (BM / 2), ROW512_DNT + kr * RK, e, &raw_full[r]);
-                    } else {
-                        mbar_expect_tx(&raw_full[r], RAW_BYTES);
-                        tma_load_3d(dst, &tm_w, kr * (RK / 2), ROW1344_DW + mt * BM, e, &raw_full[r]);
-                    }
-                }
-                if (!ok) break;
-            }
-        }
-        __syncwarp();
-    } else if (warp == W_B) {
-        // ------------------------------------------------------------ activations (B) -> ring
-        if (lane == 0) {
-            uint32_t c = 0;
-            int4 td_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT] : make_int4(0, 0, 0, 0);
-            for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
-                const int4 td = td_next;
-                if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
-                const int n0 = td.y, N = (td.z + 15) & ~15;
-                const CUtensorMap *map = N <= 16 ? &tm_b16 : N <= 32 ? &tm_b32 : N <= 64 ? &tm_b64 : &tm_b128;
-                const uint32_t bytes = (N <= 16 ? 16 : N <= 32 ? 32 : N <= 64 ? 64 : 128) * 128;
-                bool ok = true;
-                for (int kt = 0; kt < NKT; kt++, c++) {
-                    const int s = c % SB;
-                    if (!lane_wait(&b_empty[s], ((c / SB) & 1) ^ 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    mbar_expect_tx(&b_full[s], bytes);
-                    tma_load_2d(sm + OFF_B + s * B_BYTES, map, kt * BK, n0, &b_full[s]);
-                }
-                if (!ok) break;
-            }
-        }
-        __syncwarp();
-    } else if (warp == W_MMA) {
-        // ------------------------------------------------------------ tcgen05.mma issue
-        if (lane == 0) {
-            uint32_t c = 0;
-            int n_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].z : 0;
-            for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
-                const int n = n_next;
-                if (i + (int)gridDim.x < nitems) n_next = p.tiles[(i + gridDim.x) / MT].z;
-                const int a = j & 1;
-                if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
-                tc_fence_after();
-                const uint32_t idesc = instr_desc_f16((n + 15) & ~15, PH == PH_DN_T);
-                const uint32_t d = tmem + a * NT;
-                bool ok = true;
-                for (int kt = 0; kt < NKT; kt++, c++) {
-                    const int sa = c % SA, sb = c % SB;
-                    if (!lane_wait(&a_full[sa], (c / SA) & 1, abort_flag, p.status) ||
-                        !lane_wait(&b_full[sb], (c / SB) & 1, abort_flag, p.status)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a0 = sbase + OFF_A + sa * A_BYTES;
-                    const uint32_t b0 = sbase + OFF_B + sb * B_BYTES;
-#pragma unroll
-                    for (int k = 0; k < BK / 16; k++) {
-                        const uint64_t ad = smem_desc(a0 + k * 256, 128, 1024, 0);
-                        const uint64_t bd = smem_desc(b0 + k * 32, 16, 1024, 2);
-                        mma_f16(d, ad, bd, idesc, (kt | k) != 0);
-                    }
-                    mma_commit(&a_empty[sa]);
-                    mma_commit(&b_empty[sb]);
-                }
-                mma_commit(&acc_full[a]);   // also after a failed wait: tracks every MMA issued
-                if (!ok) break;
-            }
-        }
-        __syncwarp();
-    } else if (warp >= 4) {
-        // ------------------------------------------------------------ decoders: raw ring -> f16 A stages
-        const int dt = tid - 128;
-        uint32_t q = 0, c = 0;
-        // h-block exponents of the tile, one item ahead (down only)
-        int s_next = (PH != PH_UP && blockIdx.x < nitems && lane < MT_UP)
-                         ? p.tile_scale[(int64_t)(blockIdx.x / MT) * MT_UP + lane] : INT_MAX;
-        for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
-            uint32_t myfac = 0x3C003C00u;   // 1.0 in f16x2
-            if (PH != PH_UP) {
-                const int mine = s_next;
-                if (i + (int)gridDim.x < nitems && lane < MT_UP)
-                    s_next = p.tile_scale[(int64_t)((i + gridDim.x) / MT) * MT_UP + lane];
-                int s0 = mine;
-#pragma unroll
-                for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
-                myfac = lane < MT_UP ? pow2_h2(s0 - mine) : 0u;
-            }
-            const int sbf = j & 1;
-            if (!warp_wait(&slab_full[sbf], (j >> 1) & 1, lane, abort_flag, p.status)) break;
-            const uint8_t *slab = sm + OFF_SLAB + sbf * SLAB_BYTES;
-            bool ok = true;
-            for (int kr = 0; kr < NKR; kr++, q++) {
-                const int r = q % SR;
-                const int kc = min(KPR, NKT - kr * KPR);   // A stages filled from this raw stage
-                bool got = warp_wait(&raw_full[r], (q / SR) & 1, lane, abort_flag, p.status);
-                for (int t = 0; t < kc && got; t++)
-                    got = warp_wait(&a_empty[(c + t) % SA], (((c + t) / SA) & 1) ^ 1, lane, abort_flag, p.status);
-                if (!got) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t *rw = sm + OFF_RAW + r * RAW_BYTES;
-#pragma unroll
-                for (int u = 0; u < UNITS; u++) {
-                    const int unit = dt + NDEC * u;
-                    if (PH == PH_DN_T) {
-                        const int n = unit >> 2, q4 = unit & 3;   // input neuron within the stage, 32-row group
-                        const int t = n >> 6;
-                        // h block of this k-stage (128 neurons each): its factor 2^(S0 - S_block)
-                        const uint32_t f = __shfl_sync(0xffffffffu, myfac, ((kr * KPR + t) >> 1) & 31);
-                        if (t < kc) {
-                            const uint4 raw = *reinterpret_cast<const uint4 *>(rw + n * (BM / 2) + q4 * 16);
-                            const int g = (kr * RK + n) >> 4;
-                            put_mnmajor(sbase + OFF_A + ((c + t) % SA) * A_BYTES, n & 63, q4, raw,
-                                        slab + g * BM + q4 * 32, as_h2(f));
-                        }
-                    } else {
-                        const int row = unit / PPR, part = unit % PPR;   // weight row, 32-code part of the stage
-                        const int t = part >> 1;
-                        const uint32_t f = __shfl_sync(0xffffffffu, myfac, ((kr * KPR + t) >> 1) & 31);
-                        if (t < kc) {
-                            const uint4 raw = *reinterpret_cast<const uint4 *>(rw + row * (RK / 2) + part * 16);
-                            constexpr int GP = PH == PH_UP ? G_UP : G_DN;
-                            const uint16_t s01 =
-                                *reinterpret_cast<const uint16_t *>(slab + row * GP + kr * (RK / 16) + part * 2);
-                            __half2 sc = as_h2(e4m3x2_f16x2(s01));
-                            if (PH == PH_DN_O) sc = __hmul2(sc, as_h2(f));
-                            put_kmajor(sbase + OFF_A + ((c + t) % SA) * A_BYTES, row, (part & 1) * 4, raw, sc);
-                        }
-                    }
-                }
-                fence_async_smem();   // this thread's A writes -> visible to the tensor core (async proxy)
-                __syncwarp();
-                if (lane == 0) {
-                    for (int t = 0; t < kc; t++) mbar_arrive(&a_full[(c + t) % SA]);
-                    mbar_arrive(&raw_empty[r]);
-                }
-                c += kc;
-            }
-            if (!ok) break;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&slab_empty[sbf]);
-        }
-    } else {
-        // ------------------------------------------------------------ epilogue (warps 0..3 = TMEM lanes)
-        const int m = tid;
-        // no early exit: the four warps must take the same named barriers for every item
-        for (int i = blockIdx.x, j = 0; i < nitems; i += gridDim.x, j++) {
-            const int tile = i / MT, mt = i % MT;
-            const int4 td = p.tiles[tile];
-            const int e = td.x, n0 = td.y, n = td.z;
-            const int a = j & 1;
-            float *cs = colsc + a * NT;
-            const int s0 = PH != PH_UP ? tile_s0(p, tile, lane) : 0;
-            for (int jj = tid; jj < n; jj += 128) {
-                if (PH == PH_UP) cs[jj] = pow2f(-p.pair_exp[n0 + jj]) * p.s2[(int64_t)e * 2];
-                else cs[jj] = p.pair_coef[n0 + jj] * p.s2[(int64_t)e * 2 + 1] * pow2f(-s0);
-            }
-            named_sync(1, 128);
-            const bool acc_ok = warp_wait(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
-            tc_fence_after();
-            const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
-            if (PH == PH_UP) {
-                // pass 1: amax of h over the 128 x n block (every thread reaches the same barriers)
-                float mx = 0.f;
-                if (acc_ok) {
-                    for (int c0 = 0; c0 < n; c0 += 32) {
-                        float v[32];
-                        tmem_ld32(trow + c0, v);
-#pragma unroll
-                        for (int jj = 0; jj < 32; jj++) {
-                            if (c0 + jj < n) {
-                                const float u = v[jj] * cs[c0 + jj];
-                                mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                if (lane == 0) red[a * 4 + warp] = mx;
-                named_sync(1, 128);
-                mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
-                // an all-zero block takes the largest exponent so that it never sets the tile's reference
-                const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
-                if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
-                // pass 2: h * 2^S as f16 (the block's amax lands in [2^14, 2^15)), staged through shared
-                // memory 16 pairs at a time so that each pair's 128 values go out as 16-byte stores
-                const float sc = pow2f(S);
-                for (int c0 = 0; c0 < n; c0 += STG_COLS) {
-                    if (acc_ok) {
-                        float v[16];
-                        tmem_ld16(trow + c0, v);
-#pragma unroll
-                        for (int jj = 0; jj < STG_COLS; jj++) {
-                            const float u = v[jj] * cs[(c0 + jj) & (NT - 1)];
-                            stg[jj * BM + m] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
-                        }
-                    }
-                    named_sync(1, 128);
-                    if (acc_ok) {
-#pragma unroll
-                        for (int k2 = 0; k2 < 2; k2++) {
-                            const int piece = tid + 128 * k2;
-                            const int row = piece >> 4, part = piece & 15;
-                            if (c0 + row < n)
-                                *reinterpret_cast<uint4 *>(p.hs + (int64_t)(n0 + c0 + row) * INTER + mt * BM + part * 8) =
-                                    *reinterpret_cast<const uint4 *>(stg + row * BM + part * 8);
-                        }
-                    }
-                    named_sync(1, 128);
-                }
-            } else if (acc_ok) {
-                float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
-                for (int c0 = 0; c0 < n; c0 += 32) {
-                    float v[32];
-                    tmem_ld32(trow + c0, v);
-#pragma unroll
-                    for (int jj = 0; jj < 32; jj++)
-                        if (c0 + jj < n) dst[(int64_t)(c0 + jj) * LAT] = v[jj] * cs[c0 + jj];
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[a]);
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == W_MMA) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
-    }
 }
 
 // ------------------------------------------------------------------------------------------ block-scaled
@@ -840,8 +336,7 @@ struct BsPlan {
     static constexpr int STAGES = PH == PH_UP ? 5 : 4;
     static constexpr int SLAB = BM * (PH == PH_UP ? G_UP : G_DN);
     static constexpr int OFF_SLAB = STAGES * BS_STAGE;
-    static constexpr int OFF_STG = OFF_SLAB + 2 * SLAB;
-    static constexpr int OFF_COLSC = OFF_STG + STG_COLS * BM * 2;
+    static constexpr int OFF_COLSC = OFF_SLAB + 2 * SLAB;
     static constexpr int OFF_RED = OFF_COLSC + 2 * NT * 4;
     static constexpr int OFF_BAR = OFF_RED + 32;
     static constexpr int NBAR = 4 * STAGES + 8;
@@ -975,9 +470,9 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
     if (lane == 0) p.pair_exp[pr] = E;
 }
 
-// One warp per sorted pair: its h row (f16, block b scaled by 2^S_b of its tile) times 2^(S0 - HSHIFT - S_b),
-// S0 the tile's smallest block exponent, as NP planes: the planes carry h * 2^(S0 - HSHIFT) for the whole row
-// (the largest block amax lands in [2^10, 2^11), inside the e4m3 range of the plane scales).
+// One warp per sorted pair: its f32 h row times 2^(S0 - HSHIFT), S0 the tile's smallest block exponent (the
+// exponent that puts a 128-row block's amax in [2^14, 2^15), recorded by the up epilogue), as NP planes: one
+// frame for the whole row, the largest block amax in [2^10, 2^11), inside the e4m3 range of the plane scales.
 __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
     const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -986,43 +481,25 @@ __global__ void __launch_bounds__(256) pf_hplanes_kernel(const Params p) {
     const int4 td = p.tiles[tile];
     const int jrow = pr - td.y, h = b_rows(td.z);
     uint8_t *sfb = p.sfbh + (int64_t)tile * KS_DN * NP * BS_ATOM;
-    const int sb_l = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
-    int s0 = sb_l;
+    int s0 = lane < MT_UP ? p.tile_scale[(int64_t)tile * MT_UP + lane] : INT_MAX;
 #pragma unroll
     for (int o = 16; o; o >>= 1) s0 = min(s0, __shfl_xor_sync(0xffffffffu, s0, o));
     for (int g0 = 0; g0 < G_DN; g0 += 32) {   // G_DN = 168 = 4 * 42: lanes of one k-step are all in or all out
         const int grp = g0 + lane;
         const bool live = grp < G_DN;
-        const int blkid = (live ? grp : G_DN - 1) >> 3;
-        const int sbk = __shfl_sync(0xffffffffu, sb_l, blkid);
         uint8_t sc[NP] = {};
         if (live) {
             float w[16];
-            if (p.h_fp32) {   // h as computed: the frame 2^(S0 - HSHIFT) directly
-                const int d = s0 - HSHIFT;
-                const float f = d >= -126 ? pow2f(d) : 0.f;
-                const float4 *src = reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(p.hs) +
-                                                                     (int64_t)pr * INTER + grp * 16);
+            const int d = s0 - HSHIFT;   // h as computed, in the tile's frame 2^(S0 - HSHIFT)
+            const float f = d >= -126 ? pow2f(d) : 0.f;
+            const float4 *src = reinterpret_cast<const float4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float4 v = src[i];
-                    w[4 * i] = v.x * f;
-                    w[4 * i + 1] = v.y * f;
-                    w[4 * i + 2] = v.z * f;
-                    w[4 * i + 3] = v.w * f;
-                }
-            } else {          // f16 h of block b carries 2^S_b
-                const int d = s0 - HSHIFT - sbk;   // <= -HSHIFT
-                const float f = d >= -126 ? pow2f(d) : 0.f;
-                const uint4 *src = reinterpret_cast<const uint4 *>(p.hs + (int64_t)pr * INTER + grp * 16);
-                const uint4 a = src[0], b = src[1];
-                const uint32_t u[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const float2 q = __half22float2(as_h2(u[i]));
-                    w[2 * i] = q.x * f;
-                    w[2 * i + 1] = q.y * f;
-                }
+            for (int i = 0; i < 4; ++i) {
+                const float4 v = src[i];
+                w[4 * i] = v.x * f;
+                w[4 * i + 1] = v.y * f;
+                w[4 * i + 2] = v.z * f;
+                w[4 * i + 3] = v.w * f;
             }
             uint32_t codes[NP][2];
             nvfp4_planes16(w, codes, sc);
@@ -1051,24 +528,18 @@ __device__ __forceinline__ void mma_nvfp4(uint32_t tmem_d, uint64_t adesc, uint6
         : "memory");
 }
 
-// Scale-factor atom (128 rows x 4 e4m3, the layout above) from shared memory into 4 TMEM columns of all
-// 128 lanes (the 32-row pattern is broadcast to the four lane quarters).
-__device__ __forceinline__ void tmem_cp_sf(uint32_t tmem_col, uint32_t atom_addr) {
-    const uint64_t d = smem_desc(atom_addr, 16, 128, 0);
-    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(d) : "memory");
-}
-
 // Instruction descriptor of kind::mxf4nvf4: A, B e2m1 (format 1), K-major, e4m3 scales, M = 128, N = n, K = 64.
 __device__ __forceinline__ uint32_t instr_desc_nvfp4(int n) {
     return (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-// The grouped GEMM on block-scaled NVFP4 MMA; persistent, items (tile, 128 weight rows) as pf_gemm_kernel.
+// The grouped GEMM on block-scaled NVFP4 MMA; persistent: one CTA per SM walks the items (tile, 128 weight
+// rows) i = blockIdx.x, blockIdx.x + gridDim.x, ... (consecutive items share a tile, whose planes stay in L2).
 // Roles: warps 4..5 load the weight stages (TMA, 8 KB, 64-byte swizzle); warps 6..7 the NP activation planes
 // of the stage (one 3-D TMA box: planes x pair rows x 64 B) and the planes' scale atoms (one 3 KB bulk copy,
 // laid out by the plane kernels); warp 8 bulk-copies the item's 128 weight-scale rows into a slab and
 // rearranges each stage's two weight atoms from it; warps 10..13 store the stage's atoms into its TMEM scale
-// slot; warp 9 issues NP MMAs per k-step; warps 0..3 drain the other accumulator (epilogue as pf_gemm_kernel).
+// slot; warp 9 issues the MMAs into one of two TMEM accumulators while warps 0..3 drain the other (epilogue).
 // Waits of the producer and epilogue roles: between polls the thread sleeps, so that polling warps leave the
 // issue slots of their SM sub-partition to the MMA-issuing warp.
 __device__ __forceinline__ bool mbar_wait_bo(uint64_t *bar, uint32_t parity) {
@@ -1117,7 +588,6 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     const uint32_t sbase = smem_u32(sm);
     float *colsc = reinterpret_cast<float *>(sm + Plan::OFF_COLSC);
     float *red = reinterpret_cast<float *>(sm + Plan::OFF_RED);
-    __half *stg = reinterpret_cast<__half *>(sm + Plan::OFF_STG);
     uint64_t *full = reinterpret_cast<uint64_t *>(sm + Plan::OFF_BAR);
     uint64_t *empty = full + S;
     uint64_t *acc_full = empty + S;
@@ -1464,25 +934,13 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     }
                 }
             };
-            auto acc16 = [&](int c0, float(&v)[16]) {
-                tmem_ld16(trow + c0, v);
-                if (fused) {
-#pragma unroll
-                    for (int pl = 1; pl < NP; pl++) {
-                        float w[16];
-                        tmem_ld16(trow + pl * h + c0, w);
-#pragma unroll
-                        for (int jj = 0; jj < 16; jj++) v[jj] += w[jj];
-                    }
-                }
-            };
             bool released = false;
-            if (PH == PH_UP && p.h_fp32) {
+            if (PH == PH_UP) {
                 // one pass: h = relu(u)^2 stored as f32 straight from registers (thread m -> neuron m: each
                 // column is one coalesced 512-byte row segment), the block max tracked on the way; the
                 // accumulator is released as soon as its last TMEM read is done
                 float mx = 0.f;
-                float *hrow = reinterpret_cast<float *>(p.hs) + (int64_t)n0 * INTER + mt * BM + m;
+                float *hrow = p.hs + (int64_t)n0 * INTER + mt * BM + m;
                 if (acc_ok) {
                     for (int c0 = 0; c0 < n; c0 += 32) {
                         float v[32];
@@ -1508,52 +966,6 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 named_sync(1, 128);
                 mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
                 if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = mx > 0.f ? prescale_exp(mx, 15) : 127;
-            } else if (PH == PH_UP) {
-                float mx = 0.f;
-                if (acc_ok) {
-                    for (int c0 = 0; c0 < n; c0 += 32) {
-                        float v[32];
-                        acc32(c0, v);
-#pragma unroll
-                        for (int jj = 0; jj < 32; jj++) {
-                            if (c0 + jj < n) {
-                                const float u = v[jj] * cs[c0 + jj];
-                                mx = fmaxf(mx, u > 0.f ? u * u : 0.f);
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                if (lane == 0) red[a * 4 + warp] = mx;
-                named_sync(1, 128);
-                mx = fmaxf(fmaxf(red[a * 4 + 0], red[a * 4 + 1]), fmaxf(red[a * 4 + 2], red[a * 4 + 3]));
-                const int S = mx > 0.f ? prescale_exp(mx, 15) : 127;
-                if (tid == 0) p.tile_scale[(int64_t)tile * MT_UP + mt] = S;
-                const float sc = pow2f(S);
-                for (int c0 = 0; c0 < n; c0 += STG_COLS) {
-                    if (acc_ok) {
-                        float v[16];
-                        acc16(c0, v);
-#pragma unroll
-                        for (int jj = 0; jj < STG_COLS; jj++) {
-                            const float u = v[jj] * cs[(c0 + jj) & (NT - 1)];
-                            stg[jj * BM + m] = __float2half_rn((u > 0.f ? u * u : 0.f) * sc);
-                        }
-                    }
-                    named_sync(1, 128);
-                    if (acc_ok) {
-#pragma unroll
-                        for (int k2 = 0; k2 < 2; k2++) {
-                            const int piece = tid + 128 * k2;
-                            const int row = piece >> 4, part = piece & 15;
-                            if (c0 + row < n)
-                                *reinterpret_cast<uint4 *>(p.hs + (int64_t)(n0 + c0 + row) * INTER + mt * BM + part * 8) =
-                                    *reinterpret_cast<const uint4 *>(stg + row * BM + part * 8);
-                        }
-                    }
-                    named_sync(1, 128);
-                }
             } else if (acc_ok) {
                 float *dst = p.op + (int64_t)n0 * LAT + mt * BM + m;
                 for (int c0 = 0; c0 < n; c0 += 32) {
@@ -1693,7 +1105,7 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.pair_pos = take(sizeof(int) * (size_t)L.P);
     L.pair_exp = take(sizeof(int) * (size_t)L.P);
     L.tile_scale = take(sizeof(int) * (size_t)L.tiles_cap * MT_UP);
-    L.hs = take((size_t)L.P * INTER * 4);   // f32 h (orig layout); the T layout uses the first half as f16
+    L.hs = take((size_t)L.P * INTER * 4);   // f32 h
     L.op = take((size_t)L.P * LAT * 4);
     L.pair_tile = take(sizeof(int) * (size_t)L.P);
     L.xq = take((size_t)NP * L.P * (LAT / 2));
@@ -1720,19 +1132,6 @@ inline EncodeTiledFn encode_tiled() {
             fn = reinterpret_cast<EncodeTiledFn>(f);
     });
     return fn;
-}
-
-// Row-major f16 matrix [rows, cols] -> map with {64, box_rows} boxes and 128-byte swizzle.
-inline bool make_map(CUtensorMap *m, void *base, int64_t rows, int64_t cols, int box_rows) {
-    EncodeTiledFn fn = encode_tiled();
-    if (!fn) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {BK, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // The store as a u8 tensor [ne][BLOCK / pitch][pitch] (expert stride bstride), for TMA boxes of
@@ -1763,7 +1162,7 @@ inline bool make_plane_map(CUtensorMap *m, void *base, int64_t P, int row_bytes,
               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-std::atomic<uint64_t> g_smem_up{0}, g_smem_dn_t{0}, g_smem_dn_o{0};
+std::atomic<uint64_t> g_smem_up{0}, g_smem_dn_o{0};
 
 } // namespace pf
 } // namespace qmoe
@@ -1822,11 +1221,9 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.pair_pos = reinterpret_cast<int *>(ws + L.pair_pos);
     p.pair_exp = reinterpret_cast<int *>(ws + L.pair_exp);
     p.tile_scale = reinterpret_cast<int *>(ws + L.tile_scale);
-    p.xp = nullptr;
-    p.hs = reinterpret_cast<__half *>(ws + L.hs);
-    p.h_fp32 = QMOE_PF_T_F16 ? !layout_T : 1;
+    p.hs = reinterpret_cast<float *>(ws + L.hs);
     p.dconv = ws + L.dconv;
-    if (layout_T && !QMOE_PF_T_F16) {   // the down GEMM reads the converted halves
+    if (layout_T) {   // the down GEMM reads the converted halves
         p.dn_w = p.dconv;
         p.dn_sc = p.dconv + DC_W;
         p.dn_bstride = DC_STRIDE;
@@ -1844,32 +1241,23 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.sfbx = ws + L.sfbx;
     p.sfbh = ws + L.sfbh;
 
-    // up: block-scaled NVFP4 (weights as stored, x as NVFP4 planes); down: block-scaled on the orig layout,
-    // or the exact-f16 kernel on the T layout (FP4 operands of the tensor core must be K-major)
+    // both halves: block-scaled NVFP4 on the weights as stored (the down half of a T-layout store converted
+    // first), the activations as NVFP4 planes
     const int hts[4] = {16, 32, 64, 128};
-    const bool f16_down = layout_T && QMOE_PF_T_F16;
-    CUtensorMap xm[4], hm[4], bh[4], wu, wdo, wdt, sdt;
+    CUtensorMap xm[4], hm[4], wu, wdo;
     for (int k = 0; k < 4; k++) {
-        if (!make_plane_map(&xm[k], p.xq, L.P, LAT / 2, hts[k])) return QMOE_ERR_LAUNCH;
-        if (f16_down ? !make_map(&bh[k], p.hs, L.P, INTER, hts[k]) : !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
+        if (!make_plane_map(&xm[k], p.xq, L.P, LAT / 2, hts[k]) || !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
             return QMOE_ERR_LAUNCH;
     }
     if (!make_store_map(&wu, store, block_stride, n_experts, KB_UP, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;
-    if (f16_down) {
-        if (!make_store_map(&wdt, store, block_stride, n_experts, 512, BM / 2, RK) ||
-            !make_store_map(&sdt, store, block_stride, n_experts, 1024, BM, G_DN))
-            return QMOE_ERR_LAUNCH;
-    } else if (layout_T ? !make_store_map(&wdo, p.dconv, DC_STRIDE, n_experts, KB_DN, BS_BK / 2, BM,
-                                          CU_TENSOR_MAP_SWIZZLE_64B, DC_STRIDE)
-                        : !make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM,
-                                          CU_TENSOR_MAP_SWIZZLE_64B)) {
+    if (layout_T ? !make_store_map(&wdo, p.dconv, DC_STRIDE, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B,
+                                   DC_STRIDE)
+                 : !make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;
-    }
     auto up = pfb_gemm_kernel<PH_UP>;
-    if (!ensure_smem(up, BsPlan<PH_UP>::SMEM, dev, g_smem_up)) return QMOE_ERR_LAUNCH;
-    if (f16_down ? !ensure_smem(pf_gemm_kernel<PH_DN_T>, SMEM_BYTES, dev, g_smem_dn_t)
-                 : !ensure_smem(pfb_gemm_kernel<PH_DN_O>, BsPlan<PH_DN_O>::SMEM, dev, g_smem_dn_o))
+    auto dn = pfb_gemm_kernel<PH_DN_O>;
+    if (!ensure_smem(up, BsPlan<PH_UP>::SMEM, dev, g_smem_up) || !ensure_smem(dn, BsPlan<PH_DN_O>::SMEM, dev, g_smem_dn_o))
         return QMOE_ERR_LAUNCH;
 
     cudaStream_t st = as_stream(stream);
@@ -1877,17 +1265,13 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
     pf_xplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-    if (layout_T && !f16_down) {
+    if (layout_T) {
         pf_dnT_codes_kernel<<<dim3(INTER / DCV_R, LAT / 256, n_experts), 256, 0, st>>>(p);
         pf_dnT_scales_kernel<<<dim3(LAT / DCV_C, n_experts), 256, 0, st>>>(p);
     }
     up<<<di->sms, BS_THREADS, BsPlan<PH_UP>::SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
-    if (f16_down) {
-        pf_gemm_kernel<PH_DN_T><<<di->sms, THREADS, SMEM_BYTES, st>>>(p, bh[0], bh[1], bh[2], bh[3], wdt, wdt, sdt);
-    } else {
-        pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-        pfb_gemm_kernel<PH_DN_O><<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
-    }
+    pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
+    dn<<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
 }
