@@ -156,3 +156,27 @@ def test_prefill_invalid_id_poisons_only_its_token(Q, bank):
     good = [t for t in range(T) if t != 2]
     ref = oracle_prefill(b["blk_np"], b["s2_np"], ids[good], w[good], b["X_np"][good])
     assert rel_l2(yn[good], ref) < BF16_TOL
+
+
+def test_prefill_T_layout_in_cuda_graph(Q, bank):
+    """The T-layout call forks its down-half conversion onto a side stream and joins it back: recorded in a
+    CUDA graph and replayed, it gives the eager result."""
+    b = bank
+    T, k = 24, 8
+    ids, w = _route(T, 24, k, seed=41)
+    idd, wd = torch.from_numpy(ids).to(DEV), torch.from_numpy(w).to(DEV)
+    X = b["X"][:T].clone()
+    y_eager = Q.moe_prefill(b["blkT"], idd, wd, b["s2"], X, layout_T=True).clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        Q.moe_prefill(b["blkT"], idd, wd, b["s2"], X, layout_T=True)   # this stream's workspace, before capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        y_graph = Q.moe_prefill(b["blkT"], idd, wd, b["s2"], X, layout_T=True)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y_graph, y_eager)
+    del g
