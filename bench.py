@@ -195,11 +195,20 @@ def algorithmic_bytes(torch, step_bufs, L):
     return L * K * 1548288 + 1024 * groups + 512 * neurons + L * (2048 + 4096), groups, neurons
 
 
+def host_cores():
+    """Cores this process may run on (torchrun sets OMP_NUM_THREADS=1 per rank; the CPU baseline runs on rank 0
+    alone and should use all of them)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(store, s2_host, T, L, budget_s=15.0, threads=0):
     """Reference fp32 CPU expert path (oracle port) on a bounded sample: layers of token 0."""
     import numpy as np
     from oracle import oracle as O
-    n = O.max_threads() if threads <= 0 else threads
+    n = host_cores() if threads <= 0 else threads
     layers = list(range(0, L, max(1, L // 8)))
     times, used = [], []
     t_all = time.perf_counter()
@@ -230,7 +239,7 @@ def run_reference(args):
     from oracle import oracle as O
     import qmoe_synth as S
     sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
-    n = O.max_threads()
+    n = host_cores()
     # the same recipe (config 1): 4 sample layers (live fractions spread over 1-16.5%), each with 22
     # routed experts of one token, generated once on the host; a step times one layer of the
     # reference's fp32 CPU path, and the time is scaled to 40 layers per token.
