@@ -28,7 +28,7 @@ constexpr int NT = 128;                 // pairs per tile = largest MMA N used
 constexpr int BM = 128;                 // MMA M (rows of the weight tile)
 constexpr int MT_UP = INTER / BM;       // 21
 constexpr int MT_DN = LAT / BM;         // 8
-constexpr int CHUNK_T = 64;             // tokens per routing chunk
+constexpr int CHUNK_T = 16;             // tokens per routing chunk (one placement warp each)
 constexpr int MAX_NE = 1024;
 constexpr int MAX_TOPK = 32;
 constexpr int MAX_T = 65536;
@@ -72,6 +72,7 @@ struct Params {
                             // [ne][1376256 B codes | 172032 B scales]
     float *op;              // [P, 1024]
     int *pair_tile;         // [P] tile of each sorted pair
+    int *toff;              // [ne] index of the expert's first tile
     uint8_t *xq, *hq;       // [NP, P, 512], [NP, P, 1344] e2m1 codes: x, h (x 2^S0 of its tile) as NVFP4 planes
     uint8_t *sfbx, *sfbh;   // [tiles_cap, k-steps 16 | 42, NP, 512] the planes' e4m3 scales as tcgen05 atoms
 };
@@ -152,11 +153,11 @@ __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
     if (e < p.ne) {
         p.cnt[e] = cnt;
         p.eoff[e] = off;
+        p.toff[e] = toff;
         for (int i = 0; i < ntile; i++) {
             const int n0 = off + i * NT;
             p.tiles[toff + i] = make_int4(e, n0, min(NT, cnt - i * NT), 0);
         }
-        for (int i = 0; i < cnt; i++) p.pair_tile[off + i] = toff + i / NT;
     }
     if (threadIdx.x == blockDim.x - 1) {
         p.eoff[p.ne] = warp_sum[0][31];
@@ -165,7 +166,8 @@ __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
 }
 
 // One warp per chunk: walks the chunk's tokens in order and gives each (t, k) its position inside its
-// expert's run. Equal ids inside one token (not produced by a top-k router) are ranked by k.
+// expert's run, and the pair its tile. Equal ids inside one token (not produced by a top-k router) are ranked
+// by k.
 __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
     __shared__ int base[MAX_NE];
     __shared__ int sid[CHUNK_T * MAX_TOPK];
@@ -193,6 +195,7 @@ __global__ void __launch_bounds__(32) pf_place_kernel(const Params p) {
             p.pair_tok[pos] = t;
             p.pair_coef[pos] = swt[(t - t0) * p.topk + lane];
             p.pair_pos[tk] = pos;
+            p.pair_tile[pos] = p.toff[e] + (pos - p.eoff[e]) / NT;
         } else if (valid) {
             p.pair_pos[tk] = e == -1 ? -2 : -1;   // -2: no expert (skipped), -1: invalid id (NaN)
         }
@@ -1076,7 +1079,7 @@ __global__ void __launch_bounds__(256) pf_dnT_scales_kernel(const Params p) {
 
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
-    size_t status, tile_count, cnt, eoff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
+    size_t status, tile_count, cnt, eoff, toff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
         hs, op, pair_tile, xq, hq, sfbx, sfbh, dconv, total;
     int P, nchunks, tiles_cap;
 };
@@ -1098,6 +1101,7 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.tile_count = take(4);
     L.cnt = take(sizeof(int) * ne);
     L.eoff = take(sizeof(int) * (ne + 1));
+    L.toff = take(sizeof(int) * ne);
     L.chunk_hist = take(sizeof(int) * (size_t)L.nchunks * ne);
     L.tiles = take(sizeof(int4) * (size_t)L.tiles_cap);
     L.pair_tok = take(sizeof(int) * (size_t)L.P);
@@ -1214,6 +1218,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.tile_count = reinterpret_cast<int *>(ws + L.tile_count);
     p.cnt = reinterpret_cast<int *>(ws + L.cnt);
     p.eoff = reinterpret_cast<int *>(ws + L.eoff);
+    p.toff = reinterpret_cast<int *>(ws + L.toff);
     p.chunk_hist = reinterpret_cast<int *>(ws + L.chunk_hist);
     p.tiles = reinterpret_cast<int4 *>(ws + L.tiles);
     p.pair_tok = reinterpret_cast<int *>(ws + L.pair_tok);
