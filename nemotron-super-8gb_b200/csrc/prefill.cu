@@ -74,6 +74,8 @@ struct Params {
     int *pair_tile;         // [P] tile of each sorted pair
     int *toff;              // [ne] index of the expert's first tile
     uint8_t *xq, *hq;       // [NP, P, 512], [NP, P, 1344] e2m1 codes: x, h (x 2^S0 of its tile) as NVFP4 planes
+    uint8_t *xtq, *xtsc;    // [NP, T, 512] codes, [NP, T, 64] scales: x planes per token
+    int *xt_exp;            // [T] prescale exponent per token
     uint8_t *sfbx, *sfbh;   // [tiles_cap, k-steps 16 | 42, NP, 512] the planes' e4m3 scales as tcgen05 atoms
 };
 
@@ -411,18 +413,12 @@ __device__ __forceinline__ int sfb_byte(int ks, int pl, int j, int h) {
     return (ks * NP + (f ? 0 : pl)) * BS_ATOM + (r & 31) * 16 + (r >> 5) * 4;
 }
 
-// One warp per sorted pair: x[token] * 2^E (amax in [2^8, 2^9)) as NP planes; E per pair for the epilogue.
-// The codes go to xq (row-major per plane); the scales straight into the tile's atoms (sfbx), so that the
-// GEMM moves a stage's scales with one bulk copy.
-__global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
+// One warp per token: x[t] * 2^E (amax in [2^8, 2^9)) as NP planes, once per token (every pair of the token
+// uses the same planes): codes [NP][T][512 B], scales [NP][T][64 B] (lane l: groups 2l, 2l+1), E per token.
+__global__ void __launch_bounds__(256) pf_xtok_kernel(const Params p) {
     const int lane = threadIdx.x & 31;
-    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (pr >= p.eoff[p.ne]) return;
-    const int tile = p.pair_tile[pr];
-    const int4 td = p.tiles[tile];
-    const int jrow = pr - td.y, h = b_rows(td.z);
-    uint8_t *sfb = p.sfbx + (int64_t)tile * KS_UP * NP * BS_ATOM;
-    const int t = p.pair_tok[pr];
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (t >= p.T) return;
     float v[32];
     if (p.x_dtype == QMOE_DT_BF16) {
         const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(p.x) +
@@ -448,7 +444,7 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
     for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const int E = prescale_exp(amax, 9);
     const float scl = pow2f(E);
-    uint32_t sc2[NP] = {};   // this lane's two scale bytes per plane (groups 2*lane, 2*lane+1)
+    uint32_t sc2[NP] = {};
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
         float w[16];
@@ -460,17 +456,38 @@ __global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
         const int grp = 2 * lane + g;
 #pragma unroll
         for (int pl = 0; pl < NP; ++pl) {
-            *reinterpret_cast<uint2 *>(p.xq + ((int64_t)pl * p.P + pr) * (LAT / 2) + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
+            *reinterpret_cast<uint2 *>(p.xtq + ((int64_t)pl * p.T + t) * (LAT / 2) + grp * 8) = make_uint2(codes[pl][0], codes[pl][1]);
             sc2[pl] |= (uint32_t)sc[pl] << (8 * g);
         }
     }
-    // k-step ks = lane / 2 holds groups 4ks .. 4ks+3: the even lane stores all four bytes
+#pragma unroll
+    for (int pl = 0; pl < NP; ++pl)
+        *reinterpret_cast<uint16_t *>(p.xtsc + ((int64_t)pl * p.T + t) * G_UP + 2 * lane) = (uint16_t)sc2[pl];
+    if (lane == 0) p.xt_exp[t] = E;
+}
+
+// One warp per sorted pair: its token's planes copied into the pair's rows of xq (the GEMM's B operand) and
+// the token's scales placed into the tile's atoms (sfbx), so that the GEMM moves a stage's scales with one bulk
+// copy; E per pair for the epilogue.
+__global__ void __launch_bounds__(256) pf_xplanes_kernel(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int pr = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pr >= p.eoff[p.ne]) return;
+    const int tile = p.pair_tile[pr];
+    const int4 td = p.tiles[tile];
+    const int jrow = pr - td.y, h = b_rows(td.z);
+    uint8_t *sfb = p.sfbx + (int64_t)tile * KS_UP * NP * BS_ATOM;
+    const int t = p.pair_tok[pr];
 #pragma unroll
     for (int pl = 0; pl < NP; ++pl) {
-        const uint32_t hi = __shfl_down_sync(0xffffffffu, sc2[pl], 1);
-        if (!(lane & 1)) *reinterpret_cast<uint32_t *>(sfb + sfb_byte(lane >> 1, pl, jrow, h)) = sc2[pl] | (hi << 16);
+        const uint4 c = *reinterpret_cast<const uint4 *>(p.xtq + ((int64_t)pl * p.T + t) * (LAT / 2) + 16 * lane);
+        *reinterpret_cast<uint4 *>(p.xq + ((int64_t)pl * p.P + pr) * (LAT / 2) + 16 * lane) = c;
+        // k-step ks = lane / 2 holds groups 4ks .. 4ks+3: the even lane stores all four bytes
+        const uint32_t sc2 = *reinterpret_cast<const uint16_t *>(p.xtsc + ((int64_t)pl * p.T + t) * G_UP + 2 * lane);
+        const uint32_t hi = __shfl_down_sync(0xffffffffu, sc2, 1);
+        if (!(lane & 1)) *reinterpret_cast<uint32_t *>(sfb + sfb_byte(lane >> 1, pl, jrow, h)) = sc2 | (hi << 16);
     }
-    if (lane == 0) p.pair_exp[pr] = E;
+    if (lane == 0) p.pair_exp[pr] = p.xt_exp[t];
 }
 
 // One warp per sorted pair: its f32 h row times 2^(S0 - HSHIFT), S0 the tile's smallest block exponent (the
@@ -1080,7 +1097,7 @@ __global__ void __launch_bounds__(256) pf_dnT_scales_kernel(const Params p) {
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
     size_t status, tile_count, cnt, eoff, toff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
-        hs, op, pair_tile, xq, hq, sfbx, sfbh, dconv, total;
+        hs, op, pair_tile, xq, hq, sfbx, sfbh, dconv, xtq, xtsc, xt_exp, total;
     int P, nchunks, tiles_cap;
 };
 
@@ -1113,6 +1130,9 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.op = take((size_t)L.P * LAT * 4);
     L.pair_tile = take(sizeof(int) * (size_t)L.P);
     L.xq = take((size_t)NP * L.P * (LAT / 2));
+    L.xtq = take((size_t)NP * T * (LAT / 2));
+    L.xtsc = take((size_t)NP * T * G_UP);
+    L.xt_exp = take(sizeof(int) * (size_t)T);
     L.hq = take((size_t)NP * L.P * KB_DN);
     L.sfbx = take((size_t)L.tiles_cap * KS_UP * NP * BS_ATOM);
     L.dconv = take((size_t)ne * DC_STRIDE);   // T layout: converted down halves
@@ -1242,6 +1262,9 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.op = reinterpret_cast<float *>(ws + L.op);
     p.pair_tile = reinterpret_cast<int *>(ws + L.pair_tile);
     p.xq = ws + L.xq;
+    p.xtq = ws + L.xtq;
+    p.xtsc = ws + L.xtsc;
+    p.xt_exp = reinterpret_cast<int *>(ws + L.xt_exp);
     p.hq = ws + L.hq;
     p.sfbx = ws + L.sfbx;
     p.sfbh = ws + L.sfbh;
@@ -1269,6 +1292,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     pf_hist_kernel<<<L.nchunks, 256, 0, st>>>(p);
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
+    pf_xtok_kernel<<<(T + 7) / 8, 256, 0, st>>>(p);
     pf_xplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
     if (layout_T) {
         pf_dnT_codes_kernel<<<dim3(INTER / DCV_R, LAT / 256, n_experts), 256, 0, st>>>(p);
