@@ -553,7 +553,7 @@ def run_ep(args):
         line = {"metric": "MoE expert-parallel tokens/s (40-layer routed experts, top-22 of 512)",
                 "value": round(toks / ms * 1e3, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 x f16 -> f32 (tcgen05 kind::f16)",
+                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
                 "data": "synthetic",
                 "config": {"workload": f"config4: EP{world}, {T} tokens per rank, {L} layers", "layers": L,
                            "tokens_per_rank": T, "experts_per_rank": el, "parallelism": f"ep{world}",

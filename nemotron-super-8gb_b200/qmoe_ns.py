@@ -165,7 +165,10 @@ def moe_prefill(store, ids, weights, s2, X, layout_T=True, out=None):
     """Prompt-path routed-expert forward (nem_super.py:295-348 as one call): X [T,1024], ids [T,topk]
     expert ids into store [E, >= BLOCK] u8 (one block per row), weights [T,topk], s2 [E,2] f32 ->
     fp32 [T,1024] = sum over k, in k order, of weights[t,k] * expert_{ids[t,k]}(X[t]).
-    Expert-grouped GEMM on the tensor cores; layout_T: the down halves are in the T layout."""
+    One expert-grouped, block-scaled NVFP4 GEMM per half on the tensor cores (activations as three NVFP4
+    residual planes); layout_T: the down halves are in the T layout (those of the experts the prompt uses are
+    converted to the orig layout inside the call; the result equals the orig-layout call's). Ids of -1 are
+    skipped; the workspace is kept per (device, stream)."""
     if store.dtype != torch.uint8 or store.dim() != 2 or store.stride(1) != 1 or store.shape[1] < BLOCK:
         raise C.QmoeError("store must be a uint8 [E, >= BLOCK] tensor with contiguous rows")
     T, topk = ids.shape
