@@ -77,3 +77,49 @@ def test_python_mirror_refuses_cpu_tensors(L):
     blk = torch.zeros(1, qmoe_ns.BLOCK, dtype=torch.uint8)
     with pytest.raises(L.QmoeError):
         qmoe_ns.from_T_fast(blk, torch.zeros(qmoe_ns.LAT * qmoe_ns.KB_DN, dtype=torch.uint8))
+
+
+def test_prefill_and_ep_argument_checks_need_no_gpu(L):
+    """qmoe_prefill_grouped / qmoe_ep_* refuse bad arguments before touching a device, with the documented
+    codes; with valid arguments and no GPU the device check refuses (no CPU fallback)."""
+    import torch
+    lib = L.lib()
+    fake = ctypes.c_void_p(4096)          # 256-byte aligned stand-in pointer (never dereferenced)
+    BLK = 3096576
+    T, K, NE = 8, 22, 512
+    need = lib.qmoe_prefill_workspace_bytes(T, K, NE)
+    assert need > 0
+    assert lib.qmoe_prefill_workspace_bytes(0, K, NE) == 0                # T out of range
+    assert lib.qmoe_prefill_workspace_bytes(T, 33, NE) == 0               # topk > 32
+    assert lib.qmoe_prefill_workspace_bytes(2 * T, K, NE) > need         # grows with T
+
+    def pf(store=fake, stride=BLK, ne=NE, lt=1, ids=fake, w=fake, s2=fake, x=fake, dt=1, t=T, k=K, out=fake,
+           ws=fake, wsb=need):
+        return lib.qmoe_prefill_grouped(store, stride, ne, lt, ids, w, s2, x, dt, t, k, out, ws, wsb, None)
+
+    assert pf(store=None) == 5
+    assert pf(ws=None) == 5
+    assert pf(t=0) == 1
+    assert pf(k=33) == 1
+    assert pf(ne=1025) == 1
+    assert pf(stride=BLK - 16) == 1                                      # stride below one block
+    assert pf(dt=9) == 6
+    assert pf(stride=BLK + 8) == 2                                       # stride not a multiple of 16
+    assert pf(x=ctypes.c_void_p(4096 + 8)) == 2                          # activations not 16-byte aligned
+    assert pf(ws=ctypes.c_void_p(4096 + 16)) == 2                        # workspace not 256-byte aligned
+    assert pf(wsb=need - 1) == 8                                         # workspace too small
+    if not torch.cuda.is_available():
+        assert pf() == 7
+
+    def pack(x=fake, ids=fake, w=fake, t=T, k=K, ne=NE, world=8, sx=fake, sm=fake, row=fake, cnt=fake):
+        return lib.qmoe_ep_dispatch_pack(x, 1, ids, w, t, k, ne, world, sx, sm, row, cnt, None)
+
+    assert pack(x=None) == 5
+    assert pack(world=0) == 1
+    assert pack(ne=511) == 1                                             # experts do not split over 8 ranks
+    assert pack(sx=ctypes.c_void_p(4096 + 4)) == 2
+    assert lib.qmoe_ep_combine(None, fake, T, 8, fake, None) == 5
+    assert lib.qmoe_ep_combine(fake, fake, 0, 8, fake, None) == 1
+    if not torch.cuda.is_available():
+        assert pack() == 7
+        assert lib.qmoe_ep_combine(fake, fake, T, 8, fake, None) == 7
