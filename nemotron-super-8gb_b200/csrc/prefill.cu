@@ -103,30 +103,34 @@ __global__ void __launch_bounds__(256) pf_hist_kernel(const Params p) {
     for (int e = threadIdx.x; e < p.ne; e += blockDim.x) p.chunk_hist[(int64_t)blockIdx.x * p.ne + e] = hist[e];
 }
 
-// One CTA: per expert, the running offset of each chunk (in place), the expert's pair count and offset,
-// and the tile list (tiles of NT pairs, experts in ascending order).
+// One warp per expert: the running offset of each chunk (in place, chunks in order) and the expert's pair
+// count.
+__global__ void __launch_bounds__(256) pf_chunkscan_kernel(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (e >= p.ne) return;
+    int carry = 0;
+    for (int c0 = 0; c0 < p.nchunks; c0 += 32) {
+        const int c = c0 + lane;
+        const int v = c < p.nchunks ? p.chunk_hist[(int64_t)c * p.ne + e] : 0;
+        int inc = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += y;
+        }
+        if (c < p.nchunks) p.chunk_hist[(int64_t)c * p.ne + e] = carry + inc - v;
+        carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) p.cnt[e] = carry;
+}
+
+// One CTA: per expert (thread), the offset of its pairs and the tile list (tiles of NT pairs, experts in
+// ascending order).
 __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
     __shared__ int warp_sum[2][32];
     const int e = threadIdx.x;
-    int run = 0;
-    if (e < p.ne) {
-        int c = 0;
-        for (; c + 8 <= p.nchunks; c += 8) {
-            int v[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = p.chunk_hist[(int64_t)(c + i) * p.ne + e];
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                p.chunk_hist[(int64_t)(c + i) * p.ne + e] = run;
-                run += v[i];
-            }
-        }
-        for (; c < p.nchunks; c++) {
-            const int v = p.chunk_hist[(int64_t)c * p.ne + e];
-            p.chunk_hist[(int64_t)c * p.ne + e] = run;
-            run += v;
-        }
-    }
+    const int run = e < p.ne ? p.cnt[e] : 0;
     const int cnt = run;
     const int ntile = (cnt + NT - 1) / NT;
     // block exclusive scans of (cnt, ntile) in thread (= expert) order
@@ -153,7 +157,6 @@ __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
     const int off = a - cnt + (warp ? warp_sum[0][warp - 1] : 0);
     const int toff = b - ntile + (warp ? warp_sum[1][warp - 1] : 0);
     if (e < p.ne) {
-        p.cnt[e] = cnt;
         p.eoff[e] = off;
         p.toff[e] = toff;
         for (int i = 0; i < ntile; i++) {
@@ -295,6 +298,7 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 
 
 __device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+    if (mbar_try_wait(bar, parity)) return true;   // ready: no need to look at the abort flag
     const bool ok = !*abort_flag && mbar_wait(bar, parity);
     if (!ok) {
         set_error(status, DEV_ERR_TIMEOUT);
@@ -573,6 +577,7 @@ __device__ __forceinline__ bool mbar_wait_bo(uint64_t *bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ bool lane_wait_bo(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+    if (mbar_try_wait(bar, parity)) return true;
     const bool ok = !*abort_flag && mbar_wait_bo(bar, parity);
     if (!ok) {
         set_error(status, DEV_ERR_TIMEOUT);
@@ -1290,6 +1295,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
 
     cudaStream_t st = as_stream(stream);
     pf_hist_kernel<<<L.nchunks, 256, 0, st>>>(p);
+    pf_chunkscan_kernel<<<(n_experts + 7) / 8, 256, 0, st>>>(p);
     pf_scan_kernel<<<1, 1024, 0, st>>>(p);
     pf_place_kernel<<<L.nchunks, 32, 0, st>>>(p);
     pf_xtok_kernel<<<(T + 7) / 8, 256, 0, st>>>(p);
