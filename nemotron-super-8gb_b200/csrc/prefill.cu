@@ -792,7 +792,11 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     } else if (warp == BS_W_MMA) {
         // ------------------------------------------------------------ scale factors -> TMEM, NP MMAs per k-step
         if (lane == 0) {
-            uint32_t q = 0;
+            // descriptors of 64-byte-swizzled K-major tiles (LBO 16, SBO 512): the constant part once, plus the
+            // tile address / 16 (14 bits, shared memory < 256 KB)
+            const uint64_t dbase = smem_desc(0, 16, 512, 4);
+            int s = 0;
+            uint32_t ph = 0;   // stage s and the parity of its current use, advanced per stage
             int n_next = blockIdx.x < nitems ? p.tiles[blockIdx.x / MT].z : 0;
             for (int i = blockIdx.x, j = 0; i < nitems && !*abort_flag; i += gridDim.x, j++) {
                 const int n = n_next;
@@ -805,38 +809,41 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const uint32_t idesc = instr_desc_nvfp4(fused ? NP * np_ : (n + 15) & ~15);
                 const uint32_t d = tmem + a * NT;
                 const int nst = fused ? (NST + 1) / 2 : NST;   // fused tiles use wide stages
+                const uint32_t pstride = (uint32_t)(np_ * (BS_BK / 2)) >> 4;   // one plane of B, in 16-byte units
                 bool ok = true;
-                for (int kt = 0; kt < nst; kt++, q++) {
-                    const int s = q % S;
-                    if (!lane_wait(&full[s], (q / S) & 1, abort_flag, p.status) ||
-                        !lane_wait(&sf_full[s], (q / S) & 1, abort_flag, p.status)) {
+                for (int kt = 0; kt < nst; kt++) {
+                    if (!lane_wait(&full[s], ph, abort_flag, p.status) || !lane_wait(&sf_full[s], ph, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t st0 = sbase + s * BS_STAGE;
+                    const uint64_t dst0 = dbase + ((sbase + (uint32_t)s * BS_STAGE) >> 4);
                     const uint32_t slot = tmem + BS_SF_COL + s * 32;
                     if (fused) {   // all planes as one MMA: N = NP * np_ rows of B, scales in the plane-0 atom
                         const int nk = 2 * min(2, NST - 2 * kt);
                         for (int kk = 0; kk < nk; kk++) {
-                            const uint32_t half = (uint32_t)(kk >> 1), kb = (uint32_t)(kk & 1) * 32;
-                            const uint64_t ad = smem_desc(st0 + half * BS_A + kb, 16, 512, 4);
-                            const uint64_t bd = smem_desc(st0 + BW_B + half * (NP * np_ * (BS_BK / 2)) + kb, 16, 512, 4);
+                            const uint32_t half = (uint32_t)(kk >> 1), kb = (uint32_t)(kk & 1) * 2;
+                            const uint64_t ad = dst0 + half * (BS_A >> 4) + kb;
+                            const uint64_t bd = dst0 + (BW_B >> 4) + half * NP * pstride + kb;
                             mma_nvfp4(d, ad, bd, idesc, (kt | kk) != 0, slot + kk * 8, slot + kk * 8 + 4);
                         }
                     } else {
 #pragma unroll
                         for (int kk = 0; kk < BS_KS; kk++) {
                             const uint32_t sfa = slot + kk * 16;
-                            const uint64_t ad = smem_desc(st0 + kk * 32, 16, 512, 4);
+                            const uint64_t ad = dst0 + kk * 2;
 #pragma unroll
                             for (int pl = 0; pl < NP; pl++) {
-                                const uint64_t bd = smem_desc(st0 + BS_A + pl * np_ * (BS_BK / 2) + kk * 32, 16, 512, 4);
+                                const uint64_t bd = dst0 + (BS_A >> 4) + pl * pstride + kk * 2;
                                 mma_nvfp4(d, ad, bd, idesc, (kt | kk | pl) != 0, sfa, sfa + 4 + 4 * pl);
                             }
                         }
                     }
                     mma_commit(&empty[s]);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
                 mma_commit(&acc_full[a]);   // also after a failed wait: tracks every MMA issued
                 if (!ok) break;
