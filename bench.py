@@ -63,16 +63,23 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: nvidia-smi (the recipe's query, every
+    100 ms) and, so that regions of a few milliseconds still get samples, NVML read every 5 ms by a thread.
+    Both only read the GPU's state."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
     def __init__(self, index):
         self.index = index
         self.rows = []
+        self.nv = []          # (sm MHz, max MHz, reason names)
         self.p = None
+        self.nv_t = None
+        self.stop_ev = threading.Event()
+        self.nv0 = 0
 
     def start(self):
         try:
@@ -83,30 +90,77 @@ class Clocks:
             self.t.start()
         except Exception:
             self.p = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            bits = {"hw_slowdown": pynvml.nvmlClocksEventReasonHwSlowdown,
+                    "hw_thermal_slowdown": pynvml.nvmlClocksEventReasonHwThermalSlowdown,
+                    "sw_thermal_slowdown": pynvml.nvmlClocksEventReasonSwThermalSlowdown,
+                    "sw_power_cap": pynvml.nvmlClocksEventReasonSwPowerCap}
+            first = threading.Event()
+
+            def poll():
+                while not self.stop_ev.is_set():
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        mx = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.nv.append((float(sm), float(mx), [n for n, b in bits.items() if r & b]))
+                    except Exception:
+                        break
+                    finally:
+                        first.set()
+                    time.sleep(0.005)
+
+            self.nv_t = threading.Thread(target=poll, daemon=True)
+            self.nv_t.start()
+            first.wait(timeout=2.0)
+        except Exception:
+            self.nv_t = None
+        t0 = time.time()   # let nvidia-smi print its first row, so that it samples the whole region
+        while self.p is not None and not self.rows and time.time() - t0 < 1.5 and self.p.poll() is None:
+            time.sleep(0.01)
+        self.nv0 = max(len(self.nv) - 1, 0)   # NVML samples from the last one before the region on
 
     def _read(self):
         for line in self.p.stdout:
             self.rows.append([c.strip() for c in line.split(",")])
 
     def stop(self):
-        if self.p is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except Exception:
-            self.p.kill()
-        self.t.join(timeout=2)
-        sm = [float(r[1]) for r in self.rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        n_smi = len(self.rows)
+        self.stop_ev.set()
+        if self.nv_t is not None:
+            self.nv_t.join(timeout=2)
+            try:
+                import pynvml
+                pynvml.nvmlShutdown()
+            except Exception:
+                pass
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+            self.t.join(timeout=2)
+        rows = self.rows[:n_smi]
+        sm = [float(r[1]) for r in rows if len(r) > 2 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) > 2 and r[2].replace(".", "").isdigit()]
         reasons = set()
-        for r in self.rows:
-            for i, n in enumerate(names):
+        for r in rows:
+            for i, n in enumerate(self.NAMES):
                 if len(r) > 5 + i and r[5 + i] == "Active":
                     reasons.add(n)
+        for s, m, rs in self.nv[self.nv0:]:
+            sm.append(s)
+            mx.append(m)
+            reasons.update(rs)
+        if self.p is None and self.nv_t is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "nvidia_smi_samples": len(rows),
+                "nvml_samples": len(self.nv) - self.nv0}
 
 
 def build_store(torch, S, dev, n_layers, seed, layout_T=True):

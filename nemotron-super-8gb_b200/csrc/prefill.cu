@@ -618,15 +618,16 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     uint64_t *acc_full = empty + S;
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *slab_full = acc_empty + 2;
-    uint64_t *sf_full = slab_full + 2;   // [S] the stage's scale factors are in TMEM (all four store warps)
-    uint64_t *sf_src = sf_full + S;      // [S] the stage's scale atoms are in shared memory (bulk copy + weight atoms)
+    uint64_t *sf_src = slab_full + 2;    // [S] the stage's scale atoms are in shared memory (bulk copy + weight atoms)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 2);     // A and B expect_tx arrivals (codes)
+            // A and B expect_tx arrivals (codes) and one arrival per scale-store warp (the stage's scale factors
+            // are in TMEM): the MMA thread waits on this one barrier per stage
+            mbar_init(&full[s], 2 + BS_NSS);
             mbar_init(&sf_src[s], 2);   // B issuer's expect_tx for the planes' atoms, the weight-atom warp
             mbar_init(&empty[s], 1);
         }
@@ -635,7 +636,6 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             mbar_init(&acc_empty[a], 4);
             mbar_init(&slab_full[a], 1);
         }
-        for (int s = 0; s < S; s++) mbar_init(&sf_full[s], BS_NSS);
         *abort_flag = 0;
         fence_mbar_init();
     }
@@ -812,7 +812,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const uint32_t pstride = (uint32_t)(np_ * (BS_BK / 2)) >> 4;   // one plane of B, in 16-byte units
                 bool ok = true;
                 for (int kt = 0; kt < nst; kt++) {
-                    if (!lane_wait(&full[s], ph, abort_flag, p.status) || !lane_wait(&sf_full[s], ph, abort_flag, p.status)) {
+                    if (!lane_wait(&full[s], ph, abort_flag, p.status)) {
                         ok = false;
                         break;
                     }
@@ -889,7 +889,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&sf_full[s]);
+                    if (lane == 0) mbar_arrive(&full[s]);
                     continue;
                 }
                 const uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B;
@@ -908,7 +908,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sf_full[s]);
+                if (lane == 0) mbar_arrive(&full[s]);
             }
             if (!ok) break;
         }
