@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--workload", default="decode", choices=["decode", "dense", "prefill", "ep"])
     ap.add_argument("--ep-t", type=int, default=64, help="ep workload: tokens per rank per step (config 4 decode batch)")
     ap.add_argument("--prefill-t", type=int, default=2048, help="prefill workload: tokens per call (config 3)")
+    ap.add_argument("--prefill-layout", default="orig", choices=["orig", "T"],
+                    help="prefill workload: store layout (T: the down halves are converted inside the call)")
     return ap.parse_args()
 
 
@@ -407,7 +409,8 @@ PREFILL_FLOP_PER_PAIR = 2 * (2688 * 1024 + 1024 * 2688)   # up + down MACs x 2 =
 
 def run_prefill(args):
     """the prompt path, one MoE layer of 512 synthetic NVFP4 experts (orig layout, the one
-    the reference's moe_pairs reads; 1.585 GB resident in HBM), T tokens drawn as in config 0 and routed
+    the reference's moe_pairs reads, or with --prefill-layout T the T layout, whose down halves the call
+    converts first: 2 more kernels; 1.585 GB resident in HBM), T tokens drawn as in config 0 and routed
     top-22 by the synthetic router; one step = one qmoe_prefill_grouped call: routing sort, x as NVFP4
     planes (per token, then per pair), up GEMM + ReLU^2 (block-scaled NVFP4 tcgen05), h as NVFP4 planes,
     down GEMM, combine - 9 kernels. value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call
@@ -428,7 +431,8 @@ def run_prefill(args):
         tkind = "NVFP4 dense = 4 x measured cuBLAS bf16 (sustained)"
     except Exception:
         tflops, tkind = 4.0 * 1400.0, "NVFP4 dense = 4 x fallback bf16 (sustained 1.4 PF)"
-    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303, layout_T=False)
+    lt = args.prefill_layout == "T"
+    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303, layout_T=lt)
     s2l = s2[0].contiguous()
     g = S.seeded(404, dev)
     T = args.prefill_t
@@ -441,7 +445,7 @@ def run_prefill(args):
     st = torch.cuda.Stream()
     with torch.cuda.stream(st):
         for _ in range(max(3, args.warmup)):
-            Q.moe_prefill(store, ids, w, s2l, X, layout_T=False, out=out)
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=lt, out=out)
         st.synchronize()
         if Q.prefill_status() != 0:
             raise RuntimeError("prefill kernels reported a device-side error")
@@ -451,7 +455,7 @@ def run_prefill(args):
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
         for _ in range(args.steps):
-            Q.moe_prefill(store, ids, w, s2l, X, layout_T=False, out=out)
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=lt, out=out)
         e1.record(st)
         e1.synchronize()
         clocks = clk.stop()
@@ -470,7 +474,7 @@ def run_prefill(args):
             dx.copy_(hx, non_blocking=True)
             did.copy_(hid, non_blocking=True)
             dw.copy_(hw, non_blocking=True)
-            Q.moe_prefill(store, did, dw, s2l, dx, layout_T=False, out=out)
+            Q.moe_prefill(store, did, dw, s2l, dx, layout_T=lt, out=out)
             hout.copy_(out, non_blocking=True)
         e3.record(st)
         e3.synchronize()
@@ -497,12 +501,12 @@ def run_prefill(args):
             "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
             "data": "synthetic",
             "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
-                       "unique_experts": uniq, "layout": "orig", "l2": "weights (1.585 GB) exceed L2"},
+                       "unique_experts": uniq, "layout": args.prefill_layout, "l2": "weights (1.585 GB) exceed L2"},
             "roofline": roof, "clocks": clocks,
             "e2e": {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
-            "gpu_launches": 9 * args.steps}
+            "gpu_launches": (11 if lt else 9) * args.steps}
     print(json.dumps(line), flush=True)
 
 
