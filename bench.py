@@ -413,7 +413,7 @@ def run_prefill(args):
     converts first: 2 more kernels; 1.585 GB resident in HBM), T tokens drawn as in config 0 and routed
     top-22 by the synthetic router; one step = one qmoe_prefill_grouped call: routing sort, x as NVFP4
     planes (per token, then per pair), up GEMM + ReLU^2 (block-scaled NVFP4 tcgen05), h as NVFP4 planes,
-    down GEMM, combine - 9 kernels. value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call
+    down GEMM, combine - 10 kernels (routing: histogram, chunk scan, expert scan, placement). value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call
     with the token block and routing copied from pinned host memory and the output copied back, every step.
     roofline: the whole call against the slower of the HBM bound (weights of the experts hit + activations)
     and the NVFP4 tensor bound (true FLOPs at 4x the measured dense bf16 rate, the FP4:bf16 ratio of the
@@ -506,7 +506,7 @@ def run_prefill(args):
             "e2e": {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
-            "gpu_launches": (11 if lt else 9) * args.steps}
+            "gpu_launches": (12 if lt else 10) * args.steps}
     print(json.dumps(line), flush=True)
 
 
@@ -620,7 +620,7 @@ def run_ep(args):
                 "e2e": {"value": round(toks / me * 1e3, 1), "unit": "tokens/s",
                         "h2d_bytes_per_step": int(L * T * (S.LAT * 2 + K * 12)),
                         "d2h_bytes_per_step": int(L * T * S.LAT * 4)},
-                "gpu_launches": L * args.steps * (2 + 9 + 1)}
+                "gpu_launches": L * args.steps * (2 + 10 + 1)}
         print(json.dumps(line), flush=True)
     dist.barrier()
     dist.destroy_process_group()
