@@ -6,9 +6,11 @@
 // expert, nem_super.py:342-346), including the fixed-order combine over top-k (nem_super.py:309, :347).
 //
 // Pipeline (all on the caller's stream, nothing allocated):
-//   1. pf_hist / pf_scan / pf_place: a deterministic counting sort of the T*topk (token, k) pairs by
-//      expert. Pairs of one expert are contiguous and ordered by token; tiles of <= 128 pairs per expert.
-//   2. pf_xplanes: x[token] * 2^E as three NVFP4 residual planes, their scales as tcgen05 scale atoms.
+//   1. pf_hist / pf_chunkscan / pf_scan / pf_place: a deterministic counting sort of the T*topk (token, k)
+//      pairs by expert. Pairs of one expert are contiguous and ordered by token; tiles of <= 128 pairs per
+//      expert.
+//   2. pf_xtok / pf_xplanes: x[token] * 2^E as three NVFP4 residual planes (once per token), copied to each
+//      pair's rows, their scales as tcgen05 scale atoms of the pair's tile.
 //   3. (T layout only) pf_dnT_codes / pf_dnT_scales: the used experts' down halves converted to the orig
 //      (K-major) layout in the workspace.
 //   4. pfb_gemm<UP>: per (tile, 128 up rows): D = W_up (NVFP4 as stored) x planes^T, block-scaled MMA;
