@@ -291,6 +291,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload == "prefill":
+        return run_reference_prefill(args)
     import torch
     from oracle import oracle as O
     import qmoe_synth as S
@@ -333,6 +335,50 @@ def run_reference(args):
                              "sample": f"{per_step_layers} layer (22 routed experts, layers {sample_layers} "
                                        f"cycled) per step, x {L} layers"},
             "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_prefill(args):
+    """--impl reference --workload prefill: the reference's prompt path (prefill_cpu_reference) on the host
+    cores for the same workload as the prefill arm: T tokens drawn as in config 0, routed top-22 of 512 by the
+    synthetic router, one layer; each step times a bounded sample of the experts hit, scaled to all."""
+    import numpy as np
+    import torch
+    import qmoe_synth as S
+    T = args.prefill_t
+    g = S.seeded(303, "cpu")
+    m_hat = S.unit_dir(g, "cpu")
+    router = S.router(g, "cpu")
+    X = S.tokens(T, m_hat, S.seeded(404, "cpu"), "cpu")
+    ids, w = S.route(X, *router)
+    ids = ids.to(torch.int32).numpy()
+    w = w.float().numpy()
+    Xf = X.float().numpy()
+    uniq = int(np.unique(ids).size)
+    cache = {}
+    s2 = np.zeros((NE, 2), np.float32)
+
+    def block_of(e):   # synthetic expert blocks, generated once per expert sampled
+        if e not in cache:
+            blk, s2b, _ = S.expert_blocks(1, 0.0875, m_hat, S.seeded(5000 + e, "cpu"), "cpu")
+            cache[e] = blk[0].numpy()
+            s2[e] = s2b[0].numpy()
+        return cache[e]
+    samples = []
+    n = host_cores()
+    sample = ""
+    for it in range(args.warmup + args.steps):
+        v, n, sample = prefill_cpu_reference(block_of, s2, ids, w, Xf, budget_s=10.0, threads=n, max_experts=24)
+        if it >= args.warmup:
+            samples.append(v)
+    v = float(np.mean(samples))
+    line = {"impl": "reference", "metric": PREFILL_METRIC, "value": round(v, 1), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": len(samples), "warmup": args.warmup, "ms_per_step": round(T / v * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
+                       "unique_experts": uniq, "layout": "orig"},
+            "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": n, "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -405,6 +451,48 @@ def run_dense(args):
 
 
 PREFILL_FLOP_PER_PAIR = 2 * (2688 * 1024 + 1024 * 2688)   # up + down MACs x 2 = 11,010,048
+PREFILL_METRIC = "MoE prefill tokens/s (one routed-expert layer, top-22 of 512)"
+
+
+def prefill_cpu_reference(block_of, s2, ids, w, X, budget_s=15.0, threads=0, max_experts=48, return_out=False):
+    """The reference's prompt path for T > 64 (nem_super.py:342-346) on the host cores: per expert hit,
+    block_deq of its orig-layout block (the oracle's C restatement of qmoe_ns.py:407-412, fp32), then
+    relu(F.linear(x, up))^2 and F.linear(h, down) on the expert's tokens in fp32 torch with all host threads,
+    weighted and index-added into the output. A bounded sample: experts spread evenly over the ones hit (at
+    most max_experts, or what the time budget allows), their times scaled to all experts hit.
+    block_of(e) -> expert e's block as a numpy u8 array (fetched before its timing starts); s2 [ne, 2],
+    ids [T, k] (-1 = none), w [T, k], X [T, 1024] (numpy). Returns (tokens/s, threads, sample text), and the
+    output [T, 1024] of the sampled experts with return_out (all of them when the sample covers every expert)."""
+    import numpy as np
+    import torch
+    import torch.nn.functional as F
+    from oracle import oracle as O
+    n = threads or host_cores()
+    torch.set_num_threads(n)
+    ids = np.asarray(ids)
+    T = ids.shape[0]
+    uniq = np.unique(ids[ids >= 0])
+    pick = uniq[np.linspace(0, len(uniq) - 1, min(max_experts, len(uniq))).round().astype(int)]
+    Xf = torch.from_numpy(np.ascontiguousarray(X, dtype=np.float32))
+    wf = np.asarray(w, np.float32)
+    out = torch.zeros(T, 1024)
+    times = []
+    t_all = time.perf_counter()
+    for e in pick:
+        blk = block_of(int(e))
+        tok, pos = np.nonzero(ids == e)
+        t0 = time.perf_counter()
+        u, d = O.block_deq(blk, s2[e])
+        hh = torch.relu(F.linear(Xf[tok], torch.from_numpy(u))) ** 2
+        yd = F.linear(hh, torch.from_numpy(d)) * torch.from_numpy(wf[tok, pos])[:, None]
+        out.index_add_(0, torch.from_numpy(tok), yd)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_all > budget_s:
+            break
+    total_s = float(np.mean(times)) * len(uniq)
+    res = (T / total_s, n, (f"{len(times)} of the {len(uniq)} experts hit (spread over the ids, with their tokens), "
+                            f"mean {np.mean(times) * 1e3:.1f} ms/expert scaled to all {len(uniq)}"))
+    return res + (out.numpy(),) if return_out else res
 
 
 def run_prefill(args):
@@ -495,7 +583,7 @@ def run_prefill(args):
     roof["algorithmic"] = {"flop": flop, "weight_bytes": wbytes, "activation_bytes": act_bytes,
                            "t_hbm_ms": round(t_hbm, 4), "t_tensor_ms": round(t_tc, 4),
                            "pipe_flop": 3 * flop, "pipe_tflops": round(3 * flop / ms / 1e9, 1)}
-    line = {"metric": "MoE prefill tokens/s (one routed-expert layer, top-22 of 512)", "value": round(T / ms * 1e3, 1),
+    line = {"metric": PREFILL_METRIC, "value": round(T / ms * 1e3, 1),
             "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
             "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
@@ -507,6 +595,17 @@ def run_prefill(args):
                     "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
                     "d2h_bytes_per_step": int(out.numel() * 4)},
             "gpu_launches": (12 if lt else 10) * args.steps}
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        sh = s2l.cpu().numpy()
+
+        def block_of(e):   # the orig-layout block (the reference's prompt path converts T blocks first)
+            b = store[e].cpu().numpy()
+            return O.from_T(b) if lt else b
+        v, n, sample = prefill_cpu_reference(block_of, sh, ids.cpu().numpy(), w.cpu().numpy(),
+                                             X.float().cpu().numpy())
+        line["cpu_baseline"] = {"value": round(v, 1), "unit": "tokens/s", "cores": n, "kind": "port",
+                                "sample": sample}
     print(json.dumps(line), flush=True)
 
 

@@ -1,0 +1,76 @@
+"""bench.py on the CPU: the reference arms' JSON lines (decode and prefill) carry the contract's keys, the
+prefill reference arm computes the reference's prompt path (per-expert block_deq + two fp32 linears,
+nem_super.py:342-346) and agrees with the fp64 oracle, and the clock sampler degrades to a marked
+"unavailable" record without a GPU."""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "nemotron-super-8gb_b200"))
+
+import bench  # noqa: E402
+import qmoe_synth as S  # noqa: E402
+from oracle import oracle as O  # noqa: E402
+
+KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
+        "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"}
+
+
+def _run(*argv, env=None):
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), *argv], capture_output=True, text=True,
+                       timeout=600, env=env, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    return r.stdout
+
+
+def test_prefill_reference_arm_line():
+    line = json.loads(_run("--impl", "reference", "--workload", "prefill", "--prefill-t", "64", "--steps", "1",
+                           "--warmup", "0").strip().splitlines()[-1])
+    assert KEYS <= set(line)
+    assert line["impl"] == "reference" and line["unit"] == "tokens/s" and line["higher_is_better"] is True
+    assert line["metric"] == bench.PREFILL_METRIC and line["config"]["T"] == 64 and line["value"] > 0
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_other_ranks_print_nothing():
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2")
+    assert _run("--impl", "reference", "--workload", "prefill", "--prefill-t", "64", "--steps", "1",
+                "--warmup", "0", env=env).strip() == ""
+
+
+def test_prefill_cpu_reference_matches_oracle():
+    g = S.seeded(7, "cpu")
+    m_hat = S.unit_dir(g, "cpu")
+    E, T, k = 6, 24, 3
+    blk, s2, _ = S.expert_blocks(E, 0.1, m_hat, g, "cpu")
+    blocks = blk.numpy()
+    s2 = s2.numpy()
+    X = S.tokens(T, m_hat, g, "cpu").float().numpy()
+    rng = np.random.default_rng(0)
+    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    ids[3, 1] = -1                                   # a "no expert" slot is skipped
+    w = rng.random((T, k)).astype(np.float32)
+    v, n, sample, out = bench.prefill_cpu_reference(lambda e: blocks[e], s2, ids, w, X, threads=2,
+                                                    max_experts=E, return_out=True)
+    assert v > 0 and n == 2 and f"of the {E} experts" in sample
+    ref = O.prefill(list(blocks), s2, ids, w, X)
+    rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
+    assert rel < 1e-5
+
+
+def test_clock_sampler_without_gpu():
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    c = bench.Clocks(0)
+    c.start()
+    rec = c.stop()
+    assert rec["sm_mhz"] is None or rec["sm_mhz"] > 0
+    assert "reasons" in rec
