@@ -386,6 +386,25 @@ DENSE_SHAPES = [("fp8", 4096, 4096), ("fp8", 12288, 4096), ("fp8", 4096, 8192), 
                 ("nvfp4", 2688, 4096), ("nvfp4", 4096, 2688)]
 
 
+def dense_cpu_reference(weights, budget_s=20.0):
+    """The dense GEMVs on the host: the oracle's C restatement of dense_q.py:179-188 (dequantize, then the
+    matrix-vector product; one thread, fp64 accumulation) for each (q, x) of `weights`, q the quantized-weight
+    dict with numpy arrays. Returns the per-call times in microseconds (a shape whose turn comes after the
+    time budget is spent is skipped: None)."""
+    import numpy as np
+    from oracle import oracle as O
+    out = []
+    t_all = time.perf_counter()
+    for q, x in weights:
+        if time.perf_counter() - t_all > budget_s:
+            out.append(None)
+            continue
+        t0 = time.perf_counter()
+        O.dense(q["fmt"], q["w"], q.get("sc"), float(np.asarray(q["s"]).reshape(-1)[0]), q["N"], q["K"], x)
+        out.append((time.perf_counter() - t0) * 1e6)
+    return out
+
+
 def run_dense(args):
     """dense_q GEMVs at bs = 1 (and M = 2), FP8 per-tensor and NVFP4 weights drawn
     N(0, 0.02) before quantization, bf16 x ~ N(0, 1). Each shape rotates over enough weight copies that the
@@ -399,6 +418,8 @@ def run_dense(args):
     g = S.seeded(77, dev)
     st = torch.cuda.Stream()
     res = []
+    cpu_q = []          # one weight copy per shape on the host, for the CPU baseline
+    launches = 0
     for fmt, N, K in DENSE_SHAPES:
         wbytes = N * K if fmt == "fp8" else N * K // 2 + N * K // 16
         copies = max(1, min(8, -(-256 * 2**20 // wbytes)))
@@ -413,6 +434,8 @@ def run_dense(args):
                 qs.append({"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2.reshape(1), "N": N, "K": K})
             del wf
         x = torch.randn(2, K, generator=g, device=dev).to(torch.bfloat16)
+        cpu_q.append(({k_: (v_.cpu().numpy() if torch.is_tensor(v_) else v_) for k_, v_ in qs[0].items()},
+                      x[0].float().cpu().numpy()))
         for M in (1, 2):
             with torch.cuda.stream(st):
                 for q in qs:
@@ -433,20 +456,53 @@ def run_dense(args):
                 e1.record(st)
                 e1.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (10 * reps)
+            launches += 10 * reps
             b = wbytes + M * K * 2 + M * N * 4
-            res.append({"fmt": fmt, "N": N, "K": K, "M": M, "us": round(us, 3), "GB/s": round(b / us / 1e3, 1),
-                        "frac": round(b / us / 1e3 / hbm, 4)})
+            r_ = {"fmt": fmt, "N": N, "K": K, "M": M, "us": round(us, 3), "GB/s": round(b / us / 1e3, 1),
+                  "frac": round(b / us / 1e3 / hbm, 4)}
+            if M == 1:
+                # end to end through dense_q.gemv: x from pinned host memory, y back to pinned host memory
+                hx = x[0].cpu().pin_memory()
+                dxx = torch.empty_like(x[0])
+                with torch.cuda.stream(st):
+                    y0 = D.gemv(qs[0], x[0])
+                    hy = torch.empty(y0.shape, dtype=y0.dtype).pin_memory()
+                    for _ in range(3):
+                        dxx.copy_(hx, non_blocking=True)
+                        hy.copy_(D.gemv(qs[0], dxx), non_blocking=True)
+                    e2 = torch.cuda.Event(enable_timing=True)
+                    e3 = torch.cuda.Event(enable_timing=True)
+                    e2.record(st)
+                    for r in range(reps):
+                        dxx.copy_(hx, non_blocking=True)
+                        hy.copy_(D.gemv(qs[r % copies], dxx), non_blocking=True)
+                    e3.record(st)
+                    e3.synchronize()
+                r_["e2e_us"] = round(e2.elapsed_time(e3) * 1e3 / reps, 3)
+                r_["h2d"] = int(hx.numel() * hx.element_size())
+                r_["d2h"] = int(hy.numel() * hy.element_size())
+            res.append(r_)
         del qs
         torch.cuda.empty_cache()
     tot_us = sum(r["us"] for r in res if r["M"] == 1)
+    one = [r for r in res if r["M"] == 1]
+    cpu_us = None if args.no_cpu_baseline else dense_cpu_reference(cpu_q)
     tot_b = sum((r["N"] * r["K"] if r["fmt"] == "fp8" else r["N"] * r["K"] * 9 // 16) for r in res if r["M"] == 1)
     line = {"metric": "dense_q GEMV us per call (config 2 sweep, bs=1)", "value": round(tot_us, 3), "unit": "us (sum of shapes)",
-            "n_gpus": 1, "higher_is_better": False, "dtype": "fp8/nvfp4xbf16->f32", "data": "synthetic",
+            "n_gpus": 1, "steps": 10, "warmup": 3, "ms_per_step": round(tot_us / 1e3, 6), "scaling": "weak",
+            "vs_baseline": None,
+            "higher_is_better": False, "dtype": "fp8/nvfp4xbf16->f32", "data": "synthetic",
             "config": {"workload": "config2: dense_q GEMV sweep", "shapes": [list(s_) for s_ in DENSE_SHAPES],
                        "l2": "weight copies rotated beyond L2"},
             "roofline": {"bound": "hbm", "achieved": round(tot_b / tot_us / 1e3, 1), "peak": hbm, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": round(tot_b / tot_us / 1e3 / hbm, 4)},
-            "per_shape": res}
+            "per_shape": res,
+            "e2e": {"value": round(sum(r["e2e_us"] for r in one), 3), "unit": "us (sum of shapes)",
+                    "h2d_bytes_per_step": sum(r["h2d"] for r in one), "d2h_bytes_per_step": sum(r["d2h"] for r in one)},
+            "gpu_launches": launches}
+    if cpu_us is not None and all(c is not None for c in cpu_us):
+        line["cpu_baseline"] = {"value": round(sum(cpu_us), 1), "unit": "us (sum of shapes)", "cores": 1, "kind": "port",
+                                "sample": "each bs=1 shape once: oracle dequantize + matrix-vector product (fp64)"}
     print(json.dumps(line), flush=True)
 
 

@@ -74,3 +74,20 @@ def test_clock_sampler_without_gpu():
     rec = c.stop()
     assert rec["sm_mhz"] is None or rec["sm_mhz"] > 0
     assert "reasons" in rec
+
+
+def test_dense_cpu_reference():
+    g = S.seeded(9, "cpu")
+    qs = []
+    for fmt, N, K in (("fp8", 64, 128), ("nvfp4", 48, 256)):
+        wf = torch.randn(N, K, generator=g) * 0.02
+        if fmt == "fp8":
+            codes, s_ = S.quantize_fp8(wf)
+            q = {"fmt": "fp8", "w": codes.numpy(), "s": s_.reshape(1).numpy(), "N": N, "K": K}
+        else:
+            codes, sc, s2 = S.quantize_nvfp4(wf)
+            q = {"fmt": "nvfp4", "w": codes.numpy(), "sc": sc.numpy(), "s": s2.reshape(1).numpy(), "N": N, "K": K}
+        qs.append((q, torch.randn(K, generator=g).numpy()))
+    us = bench.dense_cpu_reference(qs)
+    assert len(us) == 2 and all(u is not None and u > 0 for u in us)
+    assert bench.dense_cpu_reference(qs, budget_s=-1.0) == [None, None]   # past the budget: skipped
