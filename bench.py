@@ -293,6 +293,12 @@ def run_reference(args):
         return
     if args.workload == "prefill":
         return run_reference_prefill(args)
+    if args.workload == "dense":
+        return run_reference_dense(args)
+    if args.workload == "ep":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference engine has no expert parallelism: it "
+                          "runs every expert on one GPU (see --workload prefill / decode for its paths)"}), flush=True)
+        return
     import torch
     from oracle import oracle as O
     import qmoe_synth as S
@@ -379,6 +385,46 @@ def run_reference_prefill(args):
                        "unique_experts": uniq, "layout": "orig"},
             "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": n, "kind": "port", "sample": sample},
             "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+DENSE_METRIC = "dense_q GEMV us per call (config 2 sweep, bs=1)"
+
+
+def run_reference_dense(args):
+    """--impl reference --workload dense: the dense GEMVs' CPU restatement (dense_cpu_reference: dequantize
+    and multiply, one thread) over the config 2 shapes at bs = 1, one weight copy per shape drawn on the host
+    as the dense arm draws them (N(0, 0.02) before quantization, bf16 x ~ N(0, 1))."""
+    import numpy as np
+    import torch
+    import qmoe_synth as S
+    g = S.seeded(77, "cpu")
+    weights = []
+    for fmt, N, K in DENSE_SHAPES:
+        wf = torch.randn(N, K, generator=g) * 0.02
+        if fmt == "fp8":
+            codes, s_ = S.quantize_fp8(wf)
+            q = {"fmt": "fp8", "w": codes.numpy(), "s": s_.reshape(1).numpy(), "N": N, "K": K}
+        else:
+            codes, sc, s2 = S.quantize_nvfp4(wf)
+            q = {"fmt": "nvfp4", "w": codes.numpy(), "sc": sc.numpy(), "s": s2.reshape(1).numpy(), "N": N, "K": K}
+        del wf
+        weights.append((q, torch.randn(K, generator=g).to(torch.bfloat16).float().numpy()))
+    samples = []
+    for it in range(args.warmup + args.steps):
+        us = dense_cpu_reference(weights, budget_s=120.0)
+        if it >= args.warmup and all(u is not None for u in us):
+            samples.append(sum(us))
+    v = float(np.mean(samples))
+    line = {"impl": "reference", "metric": DENSE_METRIC, "value": round(v, 1), "unit": "us (sum of shapes)",
+            "n_gpus": args.gpus, "steps": len(samples), "warmup": args.warmup, "ms_per_step": round(v / 1e3, 3),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (oracle)",
+            "data": "synthetic",
+            "config": {"workload": "config2: dense_q GEMV sweep", "shapes": [list(s_) for s_ in DENSE_SHAPES]},
+            "cpu_baseline": {"value": round(v, 1), "unit": "us (sum of shapes)", "cores": 1, "kind": "port",
+                             "sample": "each bs=1 shape once per step: oracle dequantize + matrix-vector product"},
+            "e2e": {"value": round(v, 1), "unit": "us (sum of shapes)", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -488,7 +534,7 @@ def run_dense(args):
     one = [r for r in res if r["M"] == 1]
     cpu_us = None if args.no_cpu_baseline else dense_cpu_reference(cpu_q)
     tot_b = sum((r["N"] * r["K"] if r["fmt"] == "fp8" else r["N"] * r["K"] * 9 // 16) for r in res if r["M"] == 1)
-    line = {"metric": "dense_q GEMV us per call (config 2 sweep, bs=1)", "value": round(tot_us, 3), "unit": "us (sum of shapes)",
+    line = {"metric": DENSE_METRIC, "value": round(tot_us, 3), "unit": "us (sum of shapes)",
             "n_gpus": 1, "steps": 10, "warmup": 3, "ms_per_step": round(tot_us / 1e3, 6), "scaling": "weak",
             "vs_baseline": None,
             "higher_is_better": False, "dtype": "fp8/nvfp4xbf16->f32", "data": "synthetic",

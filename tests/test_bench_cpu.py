@@ -91,3 +91,12 @@ def test_dense_cpu_reference():
     us = bench.dense_cpu_reference(qs)
     assert len(us) == 2 and all(u is not None and u > 0 for u in us)
     assert bench.dense_cpu_reference(qs, budget_s=-1.0) == [None, None]   # past the budget: skipped
+
+
+def test_dense_and_ep_reference_arms():
+    line = json.loads(_run("--impl", "reference", "--workload", "dense", "--steps", "1", "--warmup", "0")
+                      .strip().splitlines()[-1])
+    assert KEYS <= set(line)
+    assert line["metric"] == bench.DENSE_METRIC and line["higher_is_better"] is False and line["value"] > 0
+    ep = json.loads(_run("--impl", "reference", "--workload", "ep", "--steps", "1", "--warmup", "0").strip())
+    assert ep["impl"] == "reference" and "unavailable" in ep
