@@ -106,13 +106,21 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
  * any work. The first call on a device looks up the array's device address (once per device), so make
  * that first call before any stream capture. All calls share the one array: calls that overlap on the GPU
  * (other streams, other host threads) race and corrupt each other's results, so serialise them. The
- * arrival counters that must start at zero are cleared on every call; the other contents are rewritten.
+ * arrival counters that must start at zero are cleared on every call and the live masks are rewritten; the
+ * status word is not: it keeps the first device-side error of the calls since it was last cleared (a tab entry
+ * that is null or not 16-byte aligned records QMOE_ERR_ALIGN and makes that expert's part row, and so y, NaN)
+ * until qmoe_decode_groups_static_status reads and clears it.
  * Arguments and outputs as qmoe_decode_groups, without the workspace. */
 #define QMOE_STATIC_SCRATCH_BYTES 32768
 #define QMOE_STATIC_MAX_K 96
 int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
                               const int64_t *tab, const float *s2, const float *coef, const void *x, int x_dtype,
                               int K, float *h, int32_t *gidx, int32_t *gcnt, float *part, float *y, void *stream);
+
+/* No counterpart in the reference. The status word of qmoe_decode_groups_static's static array on the current
+ * device: waits for `stream`, returns QMOE_OK or the first error recorded since the last clear, and with
+ * clear != 0 resets it. Allocates nothing. */
+int qmoe_decode_groups_static_status(int clear, void *stream);
 
 /* Replaces `moe_decode` (qmoe_ns.py:70-76), the orig-layout decode forward (full down, no skip):
  * h [K,2688] f32 out, out [K,1024] f32 out (out[j] = coef[j]*s2[j,1]*D_j h_j), y [1024] = sum_j out[j]
@@ -142,10 +150,11 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
  * exactly); out [T,1024] f32. Id -1 means "no expert" (the pair is skipped; expert-parallel blocks use it for
  * experts on other ranks); any other id outside [0, n_experts) records QMOE_ERR_SHAPE in the workspace status
  * and makes that token's output NaN. 1 <= T <= 65536, 1 <= topk <= 32, 1 <= n_experts <= 1024.
- * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts) bytes, 256-byte aligned) holds the
- * sorted pairs, their activation planes, the h rows and room for n_experts converted down halves (1.55 MB
- * each, used for a T-layout store); its status word must start at zero. */
-size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts);
+ * The workspace (qmoe_prefill_workspace_bytes(T, topk, n_experts, layout_T) bytes, 256-byte aligned) holds
+ * the sorted pairs, their activation planes, the h rows and, for a T-layout store only, room for the converted
+ * down halves of the experts the prompt can use (min(n_experts, T*topk) of them, 1.55 MB each); its status
+ * word must start at zero. */
+size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts, int layout_T);
 int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
                          const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
                          void *workspace, size_t workspace_bytes, void *stream);

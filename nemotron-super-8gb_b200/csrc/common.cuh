@@ -76,6 +76,18 @@ __device__ __forceinline__ float e4m3_f32(uint8_t b) {
 __device__ __forceinline__ __half2 as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 __device__ __forceinline__ uint32_t h2_as_u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 
+// c_lo += a.lo * b.lo and c_hi += a.hi * b.hi for two f16x2 words, in fp32 (fma.rn.f32.f16: both f16 operands
+// are widened exactly, so the product is exact and the one rounding is the fp32 add).
+__device__ __forceinline__ void fma2_f16_f32(uint32_t a, uint32_t b, float &c_lo, float &c_hi) {
+    asm("{\n\t.reg .b16 al, ah, bl, bh;\n\t"
+        "mov.b32 {al, ah}, %2;\n\t"
+        "mov.b32 {bl, bh}, %3;\n\t"
+        "fma.rn.f32.f16 %0, al, bl, %0;\n\t"
+        "fma.rn.f32.f16 %1, ah, bh, %1;\n\t}"
+        : "+f"(c_lo), "+f"(c_hi)
+        : "r"(a), "r"(b));
+}
+
 // f16x2 -> (lo + hi) in fp32.
 __device__ __forceinline__ float h2sum_f32(__half2 a) {
     float2 f = __half22float2(a);

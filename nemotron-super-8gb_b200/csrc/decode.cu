@@ -22,7 +22,7 @@ namespace qmoe {
 // ------------------------------------------------------------------ up
 constexpr int UP_ROWS = 8;                          // rows per tile: half of a 16-neuron group
 constexpr int UP_HALVES = INTER / UP_ROWS;          // 336 tiles per expert
-constexpr int UP_NW = 16;                           // warps per CTA (one CTA per SM)
+constexpr int UP_NW = 12;                           // warps per CTA (one CTA per SM)
 constexpr int UP_THREADS = 32 * UP_NW;
 constexpr int UP_MAXK = 64;                         // experts whose metadata is staged in shared memory
 
@@ -48,6 +48,17 @@ struct UpTile {      // one lane's share of an 8-row tile: 16 B of codes and 2 s
     uint16_t sc[UP_ROWS];
 };
 
+// A lane's slice [32*lane, 32*lane+32) of x: as f16x2 scaled by 2^E (bf16 / f16 activations, exact) or as
+// fp32 pairs (fp32 activations, kept exact).
+template <bool XF32>
+struct UpX {
+    uint32_t h[16];
+};
+template <>
+struct UpX<true> {
+    float2 f[16];
+};
+
 __device__ __forceinline__ void up_load(const uint8_t *base, int hg, int lane, UpTile &T) {
     const uint8_t *wr = base + O_UW + (int64_t)hg * (UP_ROWS * KB_UP) + 16 * lane;
     const uint8_t *sr = base + O_US + (int64_t)hg * (UP_ROWS * G_UP) + 2 * lane;
@@ -58,43 +69,40 @@ __device__ __forceinline__ void up_load(const uint8_t *base, int hg, int lane, U
     }
 }
 
-// One 8-row tile of `_up` (qmoe_ns.py:24-44) from a lane's share of its codes and scales: decode with
-// cvt.e2m1x2, HFMA2 per 16-element group against the prescaled x slice, fp32 group scaling, 9-shuffle
-// butterfly over the 8 rows, then ReLU^2, h, the tile's 8-bit live-neuron mask and the L2 prefetch of the
-// live neurons' down rows. Shared by both up kernels, so they give bit-identical h.
+// One row's partial for a lane: its two 16-element groups (codes of words x, y and of words z, w), each summed
+// in fp32 from exact e2m1 * x products (fma.rn.f32.f16, or f32 FMAs for fp32 x), times its e4m3 scale.
+template <bool XF32>
+__device__ __forceinline__ float up_row(const uint4 w, uint16_t sc, const UpX<XF32> &x) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    float g[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t o[4];
+        e2m1x8_f16x2(ww[q], o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            if constexpr (XF32) {
+                const float2 c = __half22float2(as_h2(o[e]));
+                g[q >> 1][0] = fmaf(c.x, x.f[4 * q + e].x, g[q >> 1][0]);
+                g[q >> 1][1] = fmaf(c.y, x.f[4 * q + e].y, g[q >> 1][1]);
+            } else {
+                fma2_f16_f32(o[e], x.h[4 * q + e], g[q >> 1][0], g[q >> 1][1]);
+            }
+        }
+    }
+    const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(sc)));
+    return (g[0][0] + g[0][1]) * sf.x + (g[1][0] + g[1][1]) * sf.y;
+}
+
+// One 8-row tile of `_up` (qmoe_ns.py:24-44) from a lane's share of its codes and scales: per row the lane's two
+// 16-element groups in fp32 (as the reference accumulates), a 9-shuffle butterfly over the 8 rows, then ReLU^2,
+// h, the tile's 8-bit live-neuron mask and the L2 prefetch of the live neurons' down rows.
+template <bool XF32>
 __device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int j, int hg, float mult, bool bad,
-                                        const uint32_t (&xr)[16], int lane, const uint8_t *const *s_tab) {
+                                        const UpX<XF32> &x, int lane, const uint8_t *const *s_tab) {
     float part[UP_ROWS];
 #pragma unroll
-    for (int r = 0; r < UP_ROWS; ++r) {
-        const uint4 w = cur.w[r];
-        __half2 a0 = __float2half2_rn(0.f), a1 = a0, b0 = a0, b1 = a0;
-        uint32_t o[4];
-        e2m1x8_f16x2(w.x, o);
-        a0 = __hfma2(as_h2(o[0]), as_h2(xr[0]), a0);
-        b0 = __hfma2(as_h2(o[1]), as_h2(xr[1]), b0);
-        a0 = __hfma2(as_h2(o[2]), as_h2(xr[2]), a0);
-        b0 = __hfma2(as_h2(o[3]), as_h2(xr[3]), b0);
-        e2m1x8_f16x2(w.y, o);
-        a0 = __hfma2(as_h2(o[0]), as_h2(xr[4]), a0);
-        b0 = __hfma2(as_h2(o[1]), as_h2(xr[5]), b0);
-        a0 = __hfma2(as_h2(o[2]), as_h2(xr[6]), a0);
-        b0 = __hfma2(as_h2(o[3]), as_h2(xr[7]), b0);
-        e2m1x8_f16x2(w.z, o);
-        a1 = __hfma2(as_h2(o[0]), as_h2(xr[8]), a1);
-        b1 = __hfma2(as_h2(o[1]), as_h2(xr[9]), b1);
-        a1 = __hfma2(as_h2(o[2]), as_h2(xr[10]), a1);
-        b1 = __hfma2(as_h2(o[3]), as_h2(xr[11]), b1);
-        e2m1x8_f16x2(w.w, o);
-        a1 = __hfma2(as_h2(o[0]), as_h2(xr[12]), a1);
-        b1 = __hfma2(as_h2(o[1]), as_h2(xr[13]), b1);
-        a1 = __hfma2(as_h2(o[2]), as_h2(xr[14]), a1);
-        b1 = __hfma2(as_h2(o[3]), as_h2(xr[15]), b1);
-        const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(cur.sc[r])));
-        const float2 fa = __half22float2(__hadd2(a0, b0));   // group 2*lane
-        const float2 fb = __half22float2(__hadd2(a1, b1));   // group 2*lane+1
-        part[r] = (fa.x + fa.y) * sf.x + (fb.x + fb.y) * sf.y;
-    }
+    for (int r = 0; r < UP_ROWS; ++r) part[r] = up_row<XF32>(cur.w[r], cur.sc[r], x);
     // butterfly: 8 row partials over 32 lanes -> lanes 4r..4r+3 hold row r
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -127,7 +135,8 @@ __device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int 
         // The down kernel reads, per live neuron, its 512-byte row of dnT_w and, per live group, the
         // group's 1024-byte row of dnT_s: start bringing them into L2 now, while the up stream runs.
         const uint8_t *tb = a.tab ? (j < UP_MAXK ? s_tab[j] : reinterpret_cast<const uint8_t *>(a.tab[j])) : nullptr;
-        if (tb && !bad && m) {
+        // a null or unaligned block address is the down kernel's error case: nothing to bring in
+        if (tb && (reinterpret_cast<uintptr_t>(tb) & 15u) == 0 && !bad && m) {
             if (lead && hv > 0.f) {
                 const uint8_t *row = tb + O_DW + (int64_t)(hg * UP_ROWS + (lane >> 2)) * (LAT / 2);
 #pragma unroll
@@ -138,11 +147,10 @@ __device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int 
     }
 }
 
-// A lane's 32-element slice [32*lane, 32*lane+32) of x as f16x2, scaled by 2^E (amax*2^E in [256, 512), so
-// each 16-element group sum of exact e2m1*x products stays below 2^16); inv = 2^-E.
-__device__ __forceinline__ void up_prep_x(const UpArgs &a, int lane, uint32_t (&xr)[16], float &inv) {
-    // x slice [32*lane, 32*lane+32) as f16x2 scaled by 2^E: amax*2^E in [256, 512), so each
-    // 16-element group sum of exact e2m1*x products stays below 2^16
+// A lane's 32-element slice [32*lane, 32*lane+32) of x. bf16 / f16: as f16x2 scaled by 2^E with amax*2^E in
+// [256, 512) (exact: a bf16 or f16 value scaled by a power of two stays an f16 value), inv = 2^-E. fp32: as is.
+template <bool XF32>
+__device__ __forceinline__ void up_prep_x(const UpArgs &a, int lane, UpX<XF32> &x, float &inv) {
     float xv[32];
     if (a.x_dtype == QMOE_DT_BF16 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
         const uint4 *xp = reinterpret_cast<const uint4 *>(reinterpret_cast<const __nv_bfloat16 *>(a.x) + 32 * lane);
@@ -160,26 +168,38 @@ __device__ __forceinline__ void up_prep_x(const UpArgs &a, int lane, uint32_t (&
 #pragma unroll
         for (int i = 0; i < 32; ++i) xv[i] = load_act(a.x, a.x_dtype, 32 * lane + i);
     }
-    float am = 0.f;
+    if constexpr (XF32) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(xv[i]));
+        for (int k = 0; k < 16; ++k) x.f[k] = make_float2(xv[2 * k], xv[2 * k + 1]);
+        inv = 1.f;
+    } else {
+        float am = 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-    const int E = prescale_exp(am, 9);
-    const float pe = pow2f(E);
+        for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(xv[i]));
 #pragma unroll
-    for (int k = 0; k < 16; ++k)
-        xr[k] = h2_as_u(__halves2half2(__float2half_rn(xv[2 * k] * pe), __float2half_rn(xv[2 * k + 1] * pe)));
-    inv = pow2f(-E);
+        for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const int E = prescale_exp(am, 9);
+        const float pe = pow2f(E);
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            x.h[k] = h2_as_u(__halves2half2(__float2half_rn(xv[2 * k] * pe), __float2half_rn(xv[2 * k + 1] * pe)));
+        inv = pow2f(-E);
+    }
 }
 
-// `_up` (qmoe_ns.py:24-44) for bs = 1. One CTA per SM; warp w of CTA c takes tiles c + (w + 16k)*grid
-// (tile = 8 rows). A lane owns a 32-element slice of x (prescaled f16x2 in registers) and 16 bytes of
-// each row: it issues the 8 row loads of its tile at once, decodes the e2m1 codes with cvt.e2m1x2,
-// multiplies with HFMA2 per 16-element group, scales in fp32, and the 8 row partials are reduced with
-// a 9-shuffle butterfly. Epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask for the down
-// kernel. (Measured on B200: the 34 MB stream of one layer alone takes ~8.3 us per launch; software
-// pipelining the loads, claiming tiles dynamically, or more resident warps did not shorten it.)
+struct UpRef {   // where a tile's data lives: expert j, half group hg, block base (nullptr: bad slot), multiplier
+    int j, hg;
+    const uint8_t *base;
+    float mult;
+};
+
+// `_up` (qmoe_ns.py:24-44) for bs = 1. One CTA per SM of 12 warps; warp w of CTA c takes tiles c + (w + 12k)*grid
+// (tile = 8 rows). A lane owns a 32-element slice of x and 16 bytes of each row of a tile; the loads of the
+// warp's next tile are issued before the current tile is computed (two tiles of codes in flight per lane), so
+// the fp32 arithmetic overlaps the stream. Epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask for the
+// down kernel. (Measured on B200 with 22 experts: fp32 accumulation at 12 warps with the next tile in flight runs
+// as fast as f16 group sums did at 16 warps without it; 16 and 24 warps, or no look-ahead, are 1.5-4 us slower.)
+template <bool XF32>
 __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
     __shared__ const uint8_t *s_base[UP_MAXK];   // slot base of expert j (nullptr: slot out of range)
     __shared__ float s_s2u[UP_MAXK];
@@ -199,26 +219,40 @@ __global__ void __launch_bounds__(UP_THREADS, 1) decode_up_kernel(UpArgs a) {
     __syncthreads();
     pdl_launch_dependents();
 
-    uint32_t xr[16];
+    UpX<XF32> x;
     float inv;
-    up_prep_x(a, lane, xr, inv);
+    up_prep_x<XF32>(a, lane, x, inv);
 
-    for (int t = blockIdx.x + warp * gridDim.x; t < ntiles; t += UP_NW * gridDim.x) {
-        const int j = t / UP_HALVES, hg = t - j * UP_HALVES;
-        const uint8_t *base;
-        float mult;
-        if (j < UP_MAXK) {
-            base = s_base[j];
-            mult = s_s2u[j] * inv;
+    auto ref = [&](int t) {
+        UpRef r;
+        r.j = t / UP_HALVES;
+        r.hg = t - r.j * UP_HALVES;
+        if (r.j < UP_MAXK) {
+            r.base = s_base[r.j];
+            r.mult = s_s2u[r.j] * inv;
         } else {
-            const int64_t slot = a.sidx[j];
-            base = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
-            mult = a.s2[2 * j] * inv;
+            const int64_t slot = a.sidx[r.j];
+            r.base = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
+            r.mult = a.s2[2 * r.j] * inv;
         }
-        const bool bad = base == nullptr;
-        UpTile cur;
-        if (!bad) up_load(base, hg, lane, cur);
-        up_tile(a, cur, j, hg, mult, bad, xr, lane, s_tab);
+        return r;
+    };
+    const int tstep = UP_NW * gridDim.x;
+    int t = blockIdx.x + warp * gridDim.x;
+    UpRef rn{};
+    UpTile tn;
+    if (t < ntiles) {
+        rn = ref(t);
+        if (rn.base) up_load(rn.base, rn.hg, lane, tn);
+    }
+    for (; t < ntiles; t += tstep) {
+        const UpRef rc = rn;
+        const UpTile tc = tn;
+        if (t + tstep < ntiles) {   // the next tile's loads go out before this tile's math
+            rn = ref(t + tstep);
+            if (rn.base) up_load(rn.base, rn.hg, lane, tn);
+        }
+        up_tile<XF32>(a, tc, rc.j, rc.hg, rc.mult, rc.base == nullptr, x, lane, s_tab);
     }
 }
 
@@ -475,7 +509,9 @@ static int launch_up(const UpArgs &a, cudaStream_t st, int dev, const DeviceInfo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, decode_up_kernel, a) != cudaSuccess) return QMOE_ERR_LAUNCH;
+    const cudaError_t e = a.x_dtype == QMOE_DT_F32 ? cudaLaunchKernelEx(&cfg, decode_up_kernel<true>, a)
+                                                   : cudaLaunchKernelEx(&cfg, decode_up_kernel<false>, a);
+    if (e != cudaSuccess) return QMOE_ERR_LAUNCH;
     return launch_status();
 }
 
@@ -615,8 +651,8 @@ int qmoe_decode(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const 
     g.N = LAT;
     g.K = INTER;
     static std::atomic<uint64_t> smem_done{0};
-    auto kern = gemv_kernel<1, GM_EXPERT_DOWN, 3, 1>;
-    const size_t smem = gemv_smem_bytes(1, 1, INTER);
+    auto kern = gemv_kernel<1, GM_EXPERT_DOWN, 3, 1, true>;   // h stays fp32
+    const size_t smem = gemv_smem_bytes(true, 1, INTER);
     if (!ensure_smem(kern, smem, dev, smem_done)) return QMOE_ERR_LAUNCH;
     const int rows = 64;
     kern<<<dim3(LAT / rows, K), GEMV_THREADS, smem, st>>>(g, rows);
@@ -652,10 +688,11 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
     g.M = 1;
     g.N = INTER;
     g.K = LAT;
-    static std::atomic<uint64_t> up_done{0}, dn_done{0};
-    auto kup = gemv_kernel<1, GM_PAIR_UP, 1, 1>;
-    const size_t smem_up = gemv_smem_bytes(1, 1, LAT);
-    if (!ensure_smem(kup, smem_up, dev, up_done)) return QMOE_ERR_LAUNCH;
+    static std::atomic<uint64_t> up_done{0}, up32_done{0}, dn_done{0};
+    const bool xf32 = x_dtype == QMOE_DT_F32;   // fp32 tokens are multiplied in fp32, bf16 / f16 as exact f16
+    auto kup = xf32 ? gemv_kernel<1, GM_PAIR_UP, 1, 1, true> : gemv_kernel<1, GM_PAIR_UP, 1, 1, false>;
+    const size_t smem_up = gemv_smem_bytes(xf32, 1, LAT);
+    if (!ensure_smem(kup, smem_up, dev, xf32 ? up32_done : up_done)) return QMOE_ERR_LAUNCH;
     kup<<<dim3(INTER / 128, P), GEMV_THREADS, smem_up, st>>>(g, 128);
     if (int e = launch_status()) return e;
     GemvArgs d = g;
@@ -663,8 +700,8 @@ int qmoe_pairs(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const i
     d.y = out;
     d.N = LAT;
     d.K = INTER;
-    auto kdn = gemv_kernel<1, GM_PAIR_DOWN, 3, 1>;
-    const size_t smem_dn = gemv_smem_bytes(1, 1, INTER);
+    auto kdn = gemv_kernel<1, GM_PAIR_DOWN, 3, 1, true>;   // h stays fp32
+    const size_t smem_dn = gemv_smem_bytes(true, 1, INTER);
     if (!ensure_smem(kdn, smem_dn, dev, dn_done)) return QMOE_ERR_LAUNCH;
     kdn<<<dim3(LAT / 64, P), GEMV_THREADS, smem_dn, st>>>(d, 64);
     return launch_status();
@@ -693,6 +730,16 @@ int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
     return launch_down<true>(da, st, dev, true);
+}
+
+// The status word at the start of the static array: the first device-side error of the calls since it was last
+// cleared, read (and with `clear`, reset) on `stream` after that stream's earlier work has finished.
+int qmoe_decode_groups_static_status(int clear, void *stream) {
+    int dev;
+    if (int e = current_device(&dev, nullptr)) return e;
+    uint8_t *ws = static_scratch(dev);
+    if (!ws) return QMOE_ERR_LAUNCH;
+    return qmoe_workspace_status(ws + WS_STATUS, clear, stream);
 }
 
 } // extern "C"

@@ -8,11 +8,11 @@
 
 namespace qmoe {
 
-template <int FMT, int CPL, int M>
+template <int FMT, int CPL, int M, bool VF32>
 static int launch_dense_t(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
     static std::atomic<uint64_t> done{0};
-    auto kern = gemv_kernel<FMT, GM_DENSE, CPL, M>;
-    const size_t smem = gemv_smem_bytes(FMT, M, g.K);
+    auto kern = gemv_kernel<FMT, GM_DENSE, CPL, M, VF32>;
+    const size_t smem = gemv_smem_bytes(VF32, M, g.K);
     if (smem > di.smem_optin) return QMOE_ERR_SHAPE;
     if (!ensure_smem(kern, smem, dev, done)) return QMOE_ERR_LAUNCH;
     const int unit = 2 * GEMV_WARPS;  // rows one pass of the CTA covers
@@ -24,15 +24,22 @@ static int launch_dense_t(const GemvArgs &g, cudaStream_t st, int dev, const Dev
     return launch_status();
 }
 
-template <int FMT, int CPL>
-static int launch_dense_m(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
+// fp32 activations are staged and multiplied in fp32; bf16 / f16 ones as exactly prescaled f16.
+template <int FMT, int CPL, bool VF32>
+static int launch_dense_v(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
     switch (g.M) {
-    case 1: return launch_dense_t<FMT, CPL, 1>(g, st, dev, di);
-    case 2: return launch_dense_t<FMT, CPL, 2>(g, st, dev, di);
-    case 3: return launch_dense_t<FMT, CPL, 3>(g, st, dev, di);
-    case 4: return launch_dense_t<FMT, CPL, 4>(g, st, dev, di);
+    case 1: return launch_dense_t<FMT, CPL, 1, VF32>(g, st, dev, di);
+    case 2: return launch_dense_t<FMT, CPL, 2, VF32>(g, st, dev, di);
+    case 3: return launch_dense_t<FMT, CPL, 3, VF32>(g, st, dev, di);
+    case 4: return launch_dense_t<FMT, CPL, 4, VF32>(g, st, dev, di);
     default: return QMOE_ERR_SHAPE;
     }
+}
+
+template <int FMT, int CPL>
+static int launch_dense_m(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
+    return g.x_dtype == QMOE_DT_F32 ? launch_dense_v<FMT, CPL, true>(g, st, dev, di)
+                                    : launch_dense_v<FMT, CPL, false>(g, st, dev, di);
 }
 
 template <int FMT>

@@ -2,14 +2,15 @@
 //
 // One kernel serves the reference's dense FP8 / NVFP4 GEMVs (dense_q.py:35-136), the orig-layout expert
 // down GEMV `_down` (qmoe_ns.py:47-67) and the per-pair prompt kernels `_up_pairs` / `_down_pairs`
-// (qmoe_ns.py:79-124). Design:
-//   - each CTA owns ROWS rows of one item; its vectors are converted once into shared memory as f16x2,
-//     scaled by an exact power of two (prescale_exp) so that every e2m1*x (NVFP4) product is exact in
-//     f16 and no f16 partial can overflow;
-//   - a warp streams whole rows with 16-byte non-allocating loads, all chunks of two rows in flight
-//     per lane; codes are decoded with the hardware e2m1x2 / e4m3x2 -> f16x2 converts and multiplied
-//     with packed HFMA2 over one 16-element group (NVFP4) or one 16-byte chunk (FP8), then each
-//     partial is widened to fp32, scaled by its block scale (NVFP4) and accumulated in fp32;
+// (qmoe_ns.py:79-124). Arithmetic as the reference's: codes and scales decoded exactly, every product exact,
+// every sum in fp32 ("x -> fp32, accumulation fp32", qmoe_ns.py:4). Design:
+//   - each CTA owns ROWS rows of one item; its vectors are staged once in shared memory, either as f16x2
+//     scaled by an exact power of two (bf16 / f16 activations: exact, amax*2^E in [256, 512)) or as fp32
+//     (fp32 activations and the down modes' h, which are never rounded);
+//   - a warp streams whole rows with 16-byte non-allocating loads, all chunks of two rows in flight per
+//     lane; codes are decoded with the hardware e2m1x2 / e4m3x2 -> f16x2 converts and multiplied into fp32
+//     accumulators (fma.rn.f32.f16 against the f16 vector, or fp32 FMAs against the fp32 vector); an NVFP4
+//     16-element group sum is then scaled by its block scale in fp32;
 //   - rows are reduced with warp shuffles; the item epilogue applies the fp32 multiplier (and ReLU^2).
 // The shared-memory vector layout is [m][q][chunk] of uint4 so that the 8 lanes of a quarter-warp read
 // 8 consecutive uint4 (no bank conflicts).
@@ -45,11 +46,16 @@ struct GemvArgs {
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 
+// The vector of a GEMV in shared memory: f16x2 (bf16 / f16 activations, prescaled) or fp32.
+__host__ __device__ constexpr int gemv_vec_bytes(bool vf32) { return vf32 ? 4 : 2; }
+
 // FMT 0 = FP8 e4m3 (16 elements per 16-byte chunk), 1 = NVFP4 (32 elements per chunk, 2 scales).
-template <int FMT, int MODE, int CPL, int M>
+// VF32: the vectors are staged (and multiplied) in fp32; otherwise as prescaled f16.
+template <int FMT, int MODE, int CPL, int M, bool VF32>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows_per_cta) {
-    constexpr int EPC = FMT == 1 ? 32 : 16;   // elements per chunk
-    constexpr int Q = EPC / 8;                // uint4 (8 f16) per chunk of the vector
+    constexpr int EPC = FMT == 1 ? 32 : 16;          // elements per chunk
+    constexpr int EPU = VF32 ? 4 : 8;                 // vector elements per uint4
+    constexpr int Q = EPC / EPU;                      // uint4 of the vector per chunk
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint4 *xs = reinterpret_cast<uint4 *>(smem_raw);
     __shared__ float red[GEMV_WARPS][M];
@@ -90,56 +96,55 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
     }
     if (bad) mult = __int_as_float(0x7fc00000);
 
-    // ---- vectors -> shared f16x2, prescaled by 2^E (exact)
-    // amax per vector
-    float am[M];
+    auto vec = [&](int m, int i) -> float {   // element i of vector m
+        if (MODE == GM_DENSE) return load_act(a.x, a.x_dtype, (int64_t)m * K + i);
+        if (MODE == GM_PAIR_UP) return bad ? 0.f : load_act(a.x, a.x_dtype, (int64_t)a.ptok[item] * K + i);
+        return a.hin[(int64_t)item * K + i];
+    };
+
+    // ---- vectors -> shared memory (f16x2 prescaled by 2^E, exact; or fp32 as given)
+    if constexpr (!VF32) {
+        float am[M];
 #pragma unroll
-    for (int m = 0; m < M; ++m) am[m] = 0.f;
-    for (int i = tid; i < K; i += GEMV_THREADS) {
+        for (int m = 0; m < M; ++m) am[m] = 0.f;
+        for (int i = tid; i < K; i += GEMV_THREADS) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-            float v;
-            if (MODE == GM_DENSE) v = load_act(a.x, a.x_dtype, (int64_t)m * K + i);
-            else if (MODE == GM_PAIR_UP) v = bad ? 0.f : load_act(a.x, a.x_dtype, (int64_t)a.ptok[item] * K + i);
-            else v = a.hin[(int64_t)item * K + i];
-            am[m] = fmaxf(am[m], fabsf(v));
+            for (int m = 0; m < M; ++m) am[m] = fmaxf(am[m], fabsf(vec(m, i)));
         }
-    }
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-        float v = am[m];
-        for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) red[warp][m] = v;
-    }
-    __syncthreads();
-    if (tid < M) {
-        float v = 0.f;
-        for (int i = 0; i < GEMV_WARPS; ++i) v = fmaxf(v, red[i][tid]);
-        vscale[tid] = (float)prescale_exp(v, FMT == 1 ? 9 : 3);
-    }
-    __syncthreads();
-    // write xs[m][q][c]: element pair index i (elements 2i, 2i+1) -> chunk c = i / (EPC/2), q = (i % (EPC/2)) / 4
-    uint32_t *xs32 = reinterpret_cast<uint32_t *>(smem_raw);
-    for (int i = tid; i < K / 2; i += GEMV_THREADS) {
-        const int c = i / (EPC / 2), r = i % (EPC / 2), q = r / 4, wi = r % 4;
 #pragma unroll
         for (int m = 0; m < M; ++m) {
-            float v0, v1;
-            if (MODE == GM_DENSE) {
-                v0 = load_act(a.x, a.x_dtype, (int64_t)m * K + 2 * i);
-                v1 = load_act(a.x, a.x_dtype, (int64_t)m * K + 2 * i + 1);
-            } else if (MODE == GM_PAIR_UP) {
-                const int64_t b = bad ? 0 : (int64_t)a.ptok[item] * K;
-                v0 = bad ? 0.f : load_act(a.x, a.x_dtype, b + 2 * i);
-                v1 = bad ? 0.f : load_act(a.x, a.x_dtype, b + 2 * i + 1);
-            } else {
-                v0 = a.hin[(int64_t)item * K + 2 * i];
-                v1 = a.hin[(int64_t)item * K + 2 * i + 1];
+            float v = am[m];
+            for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+            if (lane == 0) red[warp][m] = v;
+        }
+        __syncthreads();
+        if (tid < M) {
+            float v = 0.f;
+            for (int i = 0; i < GEMV_WARPS; ++i) v = fmaxf(v, red[i][tid]);
+            vscale[tid] = (float)prescale_exp(v, 9);
+        }
+        __syncthreads();
+        // xs[m][q][c] as 32-bit words: element pair i (elements 2i, 2i+1) -> chunk c = i / (EPC/2),
+        // q = (i % (EPC/2)) / 4, word i % 4
+        uint32_t *xs32 = reinterpret_cast<uint32_t *>(smem_raw);
+        for (int i = tid; i < K / 2; i += GEMV_THREADS) {
+            const int c = i / (EPC / 2), r = i % (EPC / 2), q = r / 4, wi = r % 4;
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+                const float pe = pow2f((int)vscale[m]);
+                const __half2 hv = __halves2half2(__float2half_rn(vec(m, 2 * i) * pe), __float2half_rn(vec(m, 2 * i + 1) * pe));
+                xs32[(((size_t)m * Q + q) * nch + c) * 4 + wi] = h2_as_u(hv);
             }
-            const float pe = pow2f((int)vscale[m]);
-            __half2 hv = __halves2half2(__float2half_rn(v0 * pe), __float2half_rn(v1 * pe));
-            xs32[(((size_t)m * Q + q) * nch + c) * 4 + wi] = h2_as_u(hv);
         }
+    } else {
+        // xs[m][q][c] as float2: element pair i -> chunk c = i / (EPC/2), q = (i % (EPC/2)) / 2, pair i % 2
+        float2 *xs2 = reinterpret_cast<float2 *>(smem_raw);
+        for (int i = tid; i < K / 2; i += GEMV_THREADS) {
+            const int c = i / (EPC / 2), r = i % (EPC / 2), q = r / 2, wi = r % 2;
+#pragma unroll
+            for (int m = 0; m < M; ++m) xs2[(((size_t)m * Q + q) * nch + c) * 2 + wi] = make_float2(vec(m, 2 * i), vec(m, 2 * i + 1));
+        }
+        if (tid < M) vscale[tid] = 0.f;
     }
     __syncthreads();
     float inv[M];
@@ -181,38 +186,52 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
                         uint4 xq[Q];
 #pragma unroll
                         for (int q = 0; q < Q; ++q) xq[q] = xs[((size_t)m * Q + q) * nch + c];
-                        const uint32_t *xw = reinterpret_cast<const uint32_t *>(xq);
+                        const uint32_t *xw = reinterpret_cast<const uint32_t *>(xq);   // f16x2 words
+                        const float2 *xf = reinterpret_cast<const float2 *>(xq);       // fp32 pairs
 #pragma unroll
                         for (int rr = 0; rr < 2; ++rr) {
                             const uint32_t *ww = reinterpret_cast<const uint32_t *>(&wv[rr][i]);
+                            // g[group][lo/hi]: fp32 partial sums of the chunk's one or two 16-element groups
+                            float g[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
                             if (FMT == 1) {
-                                __half2 g0 = __float2half2_rn(0.f), g1 = __float2half2_rn(0.f);
-                                uint32_t o[4];
-                                e2m1x8_f16x2(ww[0], o);
 #pragma unroll
-                                for (int k = 0; k < 4; ++k) g0 = __hfma2(as_h2(o[k]), as_h2(xw[k]), g0);
-                                e2m1x8_f16x2(ww[1], o);
+                                for (int wd = 0; wd < 4; ++wd) {   // word wd: elements 8wd .. 8wd+7
+                                    uint32_t o[4];
+                                    e2m1x8_f16x2(ww[wd], o);
 #pragma unroll
-                                for (int k = 0; k < 4; ++k) g0 = __hfma2(as_h2(o[k]), as_h2(xw[4 + k]), g0);
-                                e2m1x8_f16x2(ww[2], o);
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) g1 = __hfma2(as_h2(o[k]), as_h2(xw[8 + k]), g1);
-                                e2m1x8_f16x2(ww[3], o);
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) g1 = __hfma2(as_h2(o[k]), as_h2(xw[12 + k]), g1);
-                                const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(sv[rr][i])));
-                                acc[rr][m] = fmaf(h2sum_f32(g0), sf.x, acc[rr][m]);
-                                acc[rr][m] = fmaf(h2sum_f32(g1), sf.y, acc[rr][m]);
-                            } else {
-                                __half2 g0 = __float2half2_rn(0.f), g1 = __float2half2_rn(0.f);
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) {
-                                    uint32_t lo, hi;
-                                    e4m3x4_f16x2(ww[k], lo, hi);
-                                    g0 = __hfma2(as_h2(lo), as_h2(xw[2 * k]), g0);
-                                    g1 = __hfma2(as_h2(hi), as_h2(xw[2 * k + 1]), g1);
+                                    for (int k = 0; k < 4; ++k) {
+                                        float &lo = g[wd >> 1][0], &hi = g[wd >> 1][1];
+                                        if constexpr (VF32) {
+                                            const float2 cv = __half22float2(as_h2(o[k]));
+                                            const float2 xv = xf[4 * wd + k];
+                                            lo = fmaf(cv.x, xv.x, lo);
+                                            hi = fmaf(cv.y, xv.y, hi);
+                                        } else {
+                                            fma2_f16_f32(o[k], xw[4 * wd + k], lo, hi);
+                                        }
+                                    }
                                 }
-                                acc[rr][m] += h2sum_f32(g0) + h2sum_f32(g1);
+                                const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(sv[rr][i])));
+                                acc[rr][m] = fmaf(g[0][0] + g[0][1], sf.x, acc[rr][m]);
+                                acc[rr][m] = fmaf(g[1][0] + g[1][1], sf.y, acc[rr][m]);
+                            } else {
+#pragma unroll
+                                for (int wd = 0; wd < 4; ++wd) {   // word wd: elements 4wd .. 4wd+3
+                                    uint32_t lo2, hi2;
+                                    e4m3x4_f16x2(ww[wd], lo2, hi2);
+                                    if constexpr (VF32) {
+                                        const float2 c0 = __half22float2(as_h2(lo2)), c1 = __half22float2(as_h2(hi2));
+                                        const float2 x0 = xf[2 * wd], x1 = xf[2 * wd + 1];
+                                        g[0][0] = fmaf(c0.x, x0.x, g[0][0]);
+                                        g[0][1] = fmaf(c0.y, x0.y, g[0][1]);
+                                        g[1][0] = fmaf(c1.x, x1.x, g[1][0]);
+                                        g[1][1] = fmaf(c1.y, x1.y, g[1][1]);
+                                    } else {
+                                        fma2_f16_f32(lo2, xw[2 * wd], g[0][0], g[0][1]);
+                                        fma2_f16_f32(hi2, xw[2 * wd + 1], g[1][0], g[1][1]);
+                                    }
+                                }
+                                acc[rr][m] += (g[0][0] + g[0][1]) + (g[1][0] + g[1][1]);
                             }
                         }
                     }
@@ -245,6 +264,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
 }
 
 // shared-memory bytes of the vector copy
-inline size_t gemv_smem_bytes(int fmt, int M, int K) { return (size_t)M * (size_t)K * 2; }
+inline size_t gemv_smem_bytes(bool vf32, int M, int K) { return (size_t)M * (size_t)K * gemv_vec_bytes(vf32); }
 
 } // namespace qmoe

@@ -59,7 +59,7 @@ struct Params {
     int *cnt;               // [ne]
     int *eoff;              // [ne + 1]
     int *chunk_hist;        // [nchunks, ne] counts, then per-chunk offsets
-    int4 *tiles;            // [tiles_cap] (expert, first pair, pairs, 0)
+    int4 *tiles;            // [tiles_cap] (expert, first pair, pairs, rank of the expert among those used)
     int *pair_tok;          // [P]
     float *pair_coef;       // [P]
     int *pair_pos;          // [T * topk] sorted position of (t, k), -1 if the id was invalid
@@ -70,8 +70,10 @@ struct Params {
     const uint8_t *dn_sc;   // down scales [1024][168] of expert e at dn_sc + e * dn_bstride
     int64_t dn_bstride;
     int dn_row0;
-    uint8_t *dconv;         // T layout: the used experts' down halves converted to the orig layout
-                            // [ne][1376256 B codes | 172032 B scales]
+    uint8_t *dconv;         // T layout: the used experts' down halves converted to the orig layout,
+                            // [used experts][1376256 B codes | 172032 B scales], in ascending expert order
+    int *ecomp;             // [ne] rank of expert e among the experts with pairs (-1: no pair)
+    int dn_compact;         // 1: the down GEMM addresses its weights by the rank (tile .w), not the id
     float *op;              // [P, 1024]
     int *pair_tile;         // [P] tile of each sorted pair
     int *toff;              // [ne] index of the expert's first tile
@@ -130,40 +132,46 @@ __global__ void __launch_bounds__(256) pf_chunkscan_kernel(const Params p) {
 // One CTA: per expert (thread), the offset of its pairs and the tile list (tiles of NT pairs, experts in
 // ascending order).
 __global__ void __launch_bounds__(1024) pf_scan_kernel(const Params p) {
-    __shared__ int warp_sum[2][32];
+    __shared__ int warp_sum[3][32];
     const int e = threadIdx.x;
     const int run = e < p.ne ? p.cnt[e] : 0;
     const int cnt = run;
     const int ntile = (cnt + NT - 1) / NT;
-    // block exclusive scans of (cnt, ntile) in thread (= expert) order
+    const int used = cnt > 0;
+    // block exclusive scans of (cnt, ntile, used) in thread (= expert) order
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int a = cnt, b = ntile;
+    int a = cnt, b = ntile, c = used;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const int ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o);
-        if (lane >= o) { a += ya; b += yb; }
+        const int ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o),
+                  yc = __shfl_up_sync(0xffffffffu, c, o);
+        if (lane >= o) { a += ya; b += yb; c += yc; }
     }
-    if (lane == 31) { warp_sum[0][warp] = a; warp_sum[1][warp] = b; }
+    if (lane == 31) { warp_sum[0][warp] = a; warp_sum[1][warp] = b; warp_sum[2][warp] = c; }
     __syncthreads();
     if (warp == 0) {
-        int wa = warp_sum[0][lane], wb = warp_sum[1][lane];
+        int wa = warp_sum[0][lane], wb = warp_sum[1][lane], wc = warp_sum[2][lane];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int ya = __shfl_up_sync(0xffffffffu, wa, o), yb = __shfl_up_sync(0xffffffffu, wb, o);
-            if (lane >= o) { wa += ya; wb += yb; }
+            const int ya = __shfl_up_sync(0xffffffffu, wa, o), yb = __shfl_up_sync(0xffffffffu, wb, o),
+                      yc = __shfl_up_sync(0xffffffffu, wc, o);
+            if (lane >= o) { wa += ya; wb += yb; wc += yc; }
         }
         warp_sum[0][lane] = wa;
         warp_sum[1][lane] = wb;
+        warp_sum[2][lane] = wc;
     }
     __syncthreads();
     const int off = a - cnt + (warp ? warp_sum[0][warp - 1] : 0);
     const int toff = b - ntile + (warp ? warp_sum[1][warp - 1] : 0);
+    const int rank = c - used + (warp ? warp_sum[2][warp - 1] : 0);
     if (e < p.ne) {
         p.eoff[e] = off;
         p.toff[e] = toff;
+        p.ecomp[e] = used ? rank : -1;
         for (int i = 0; i < ntile; i++) {
             const int n0 = off + i * NT;
-            p.tiles[toff + i] = make_int4(e, n0, min(NT, cnt - i * NT), 0);
+            p.tiles[toff + i] = make_int4(e, n0, min(NT, cnt - i * NT), rank);
         }
     }
     if (threadIdx.x == blockDim.x - 1) {
@@ -661,7 +669,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             for (int i = blockIdx.x; i < nitems && !*abort_flag; i += gridDim.x) {
                 const int4 td = td_next;
                 if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
-                const int mt = i % MT, e = td.x;
+                const int mt = i % MT, e = PH == PH_DN_O && p.dn_compact ? td.w : td.x;
                 const bool wide = fused_planes(b_rows(td.z));
                 const int nst = wide ? (NST + 1) / 2 : NST;
                 bool ok = true;
@@ -730,12 +738,14 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
         uint8_t *slab = sm + Plan::OFF_SLAB;
         const uint8_t *wsc0 = PH == PH_UP ? p.store + O_US : p.dn_sc;
         const int64_t wstride = PH == PH_UP ? p.bstride : p.dn_bstride;
+        // the weight block of a tile: the expert id, or for converted down halves the expert's rank among those used
+        auto wexp = [&](const int4 &td) { return PH == PH_DN_O && p.dn_compact ? td.w : td.x; };
         uint32_t issued[2] = {0, 0}, done[2] = {0, 0};
         if (blockIdx.x < nitems) {
             if (lane == 0) {
                 const int i = blockIdx.x;
                 mbar_expect_tx(&slab_full[0], Plan::SLAB);
-                bulk_g2s_nohint(slab, wsc0 + (int64_t)p.tiles[i / MT].x * wstride + (int64_t)(i % MT) * Plan::SLAB,
+                bulk_g2s_nohint(slab, wsc0 + (int64_t)wexp(p.tiles[i / MT]) * wstride + (int64_t)(i % MT) * Plan::SLAB,
                                 Plan::SLAB, &slab_full[0]);
             }
             issued[0] = 1;
@@ -751,7 +761,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     fence_async_smem();
                     mbar_expect_tx(&slab_full[b ^ 1], Plan::SLAB);
                     bulk_g2s_nohint(slab + (b ^ 1) * Plan::SLAB,
-                                    wsc0 + (int64_t)p.tiles[inext / MT].x * wstride + (int64_t)(inext % MT) * Plan::SLAB,
+                                    wsc0 + (int64_t)wexp(p.tiles[inext / MT]) * wstride + (int64_t)(inext % MT) * Plan::SLAB,
                                     Plan::SLAB, &slab_full[b ^ 1]);
                 }
                 issued[b ^ 1]++;
@@ -1062,11 +1072,11 @@ __device__ __forceinline__ void nibble_transpose8(uint32_t (&w)[8]) {
 // and writes 4 bytes to each of its 8 output rows (8 consecutive lanes fill one 32-byte sector).
 __global__ void __launch_bounds__(256) pf_dnT_codes_kernel(const Params p) {
     __shared__ uint32_t tile[DCV_R][33];
-    const int e = blockIdx.z;
-    if (p.cnt[e] == 0) return;
+    const int e = blockIdx.z, ce = p.ecomp[e];
+    if (ce < 0) return;
     const int n0 = blockIdx.x * DCV_R, r0 = blockIdx.y * 256;
     const uint8_t *A = p.store + (int64_t)e * p.bstride + O_DW;   // [2688][512 B]
-    uint8_t *B = p.dconv + (int64_t)e * DC_STRIDE;                 // [1024][1344 B]
+    uint8_t *B = p.dconv + (int64_t)ce * DC_STRIDE;                // [1024][1344 B]
     const int tid = threadIdx.x;
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
@@ -1088,11 +1098,11 @@ __global__ void __launch_bounds__(256) pf_dnT_codes_kernel(const Params p) {
 // dnT_s [168 groups][1024 rows] -> [1024 rows][168 groups] for 128 rows per CTA.
 __global__ void __launch_bounds__(256) pf_dnT_scales_kernel(const Params p) {
     __shared__ __align__(16) uint8_t s[G_DN][DCV_C + 4];
-    const int e = blockIdx.y;
-    if (p.cnt[e] == 0) return;
+    const int e = blockIdx.y, ce = p.ecomp[e];
+    if (ce < 0) return;
     const int r0 = blockIdx.x * DCV_C;
     const uint8_t *A = p.store + (int64_t)e * p.bstride + O_DS;   // [168][1024]
-    uint8_t *B = p.dconv + (int64_t)e * DC_STRIDE + DC_W;          // [1024][168]
+    uint8_t *B = p.dconv + (int64_t)ce * DC_STRIDE + DC_W;         // [1024][168]
     for (int i = threadIdx.x; i < G_DN * (DCV_C / 16); i += blockDim.x) {
         const int g = i >> 3, part = i & 7;
         const uint4 v = *reinterpret_cast<const uint4 *>(A + (int64_t)g * LAT + r0 + 16 * part);
@@ -1110,14 +1120,14 @@ __global__ void __launch_bounds__(256) pf_dnT_scales_kernel(const Params p) {
 
 // ------------------------------------------------------------------------------------------ host
 struct WsLayout {
-    size_t status, tile_count, cnt, eoff, toff, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
+    size_t status, tile_count, cnt, eoff, toff, ecomp, chunk_hist, tiles, pair_tok, pair_coef, pair_pos, pair_exp, tile_scale,
         hs, op, pair_tile, xq, hq, sfbx, sfbh, dconv, xtq, xtsc, xt_exp, total;
     int P, nchunks, tiles_cap;
 };
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-inline WsLayout ws_layout(int T, int topk, int ne) {
+inline WsLayout ws_layout(int T, int topk, int ne, bool layout_T) {
     WsLayout L{};
     L.P = T * topk;
     L.nchunks = (T + CHUNK_T - 1) / CHUNK_T;
@@ -1133,6 +1143,7 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.cnt = take(sizeof(int) * ne);
     L.eoff = take(sizeof(int) * (ne + 1));
     L.toff = take(sizeof(int) * ne);
+    L.ecomp = take(sizeof(int) * ne);
     L.chunk_hist = take(sizeof(int) * (size_t)L.nchunks * ne);
     L.tiles = take(sizeof(int4) * (size_t)L.tiles_cap);
     L.pair_tok = take(sizeof(int) * (size_t)L.P);
@@ -1149,7 +1160,8 @@ inline WsLayout ws_layout(int T, int topk, int ne) {
     L.xt_exp = take(sizeof(int) * (size_t)T);
     L.hq = take((size_t)NP * L.P * KB_DN);
     L.sfbx = take((size_t)L.tiles_cap * KS_UP * NP * BS_ATOM);
-    L.dconv = take((size_t)ne * DC_STRIDE);   // T layout: converted down halves
+    // T layout: the converted down halves of the experts with pairs (at most min(ne, P) of them)
+    L.dconv = take(layout_T ? (size_t)(ne < L.P ? ne : L.P) * DC_STRIDE : 0);
     L.sfbh = take((size_t)L.tiles_cap * KS_DN * NP * BS_ATOM);
     L.total = o;
     return L;
@@ -1209,9 +1221,9 @@ using namespace qmoe;
 
 extern "C" {
 
-size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts) {
+size_t qmoe_prefill_workspace_bytes(int T, int topk, int n_experts, int layout_T) {
     if (T < 1 || T > pf::MAX_T || topk < 1 || topk > pf::MAX_TOPK || n_experts < 1 || n_experts > pf::MAX_NE) return 0;
-    return pf::ws_layout(T, topk, n_experts).total;
+    return pf::ws_layout(T, topk, n_experts, layout_T != 0).total;
 }
 
 int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_experts, int layout_T, const int32_t *ids,
@@ -1226,7 +1238,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     if ((block_stride & 15) || !aligned16(store) || !aligned16(x) || !aligned16(out) || !aligned4(ids) ||
         !aligned4(weights) || !aligned4(s2) || (reinterpret_cast<uintptr_t>(workspace) & 255u))
         return QMOE_ERR_ALIGN;
-    const WsLayout L = ws_layout(T, topk, n_experts);
+    const WsLayout L = ws_layout(T, topk, n_experts, layout_T != 0);
     if (workspace_bytes < L.total) return QMOE_ERR_WORKSPACE;
     int dev;
     DeviceInfo *di;
@@ -1253,6 +1265,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.cnt = reinterpret_cast<int *>(ws + L.cnt);
     p.eoff = reinterpret_cast<int *>(ws + L.eoff);
     p.toff = reinterpret_cast<int *>(ws + L.toff);
+    p.ecomp = reinterpret_cast<int *>(ws + L.ecomp);
     p.chunk_hist = reinterpret_cast<int *>(ws + L.chunk_hist);
     p.tiles = reinterpret_cast<int4 *>(ws + L.tiles);
     p.pair_tok = reinterpret_cast<int *>(ws + L.pair_tok);
@@ -1267,6 +1280,7 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
         p.dn_sc = p.dconv + DC_W;
         p.dn_bstride = DC_STRIDE;
         p.dn_row0 = 0;
+        p.dn_compact = 1;
     } else {
         p.dn_w = store;
         p.dn_sc = store + O_DS;
@@ -1293,7 +1307,8 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     }
     if (!make_store_map(&wu, store, block_stride, n_experts, KB_UP, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;
-    if (layout_T ? !make_store_map(&wdo, p.dconv, DC_STRIDE, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B,
+    const int n_conv = n_experts < L.P ? n_experts : L.P;   // converted halves: one per expert with pairs
+    if (layout_T ? !make_store_map(&wdo, p.dconv, DC_STRIDE, n_conv, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B,
                                    DC_STRIDE)
                  : !make_store_map(&wdo, store, block_stride, n_experts, KB_DN, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
         return QMOE_ERR_LAUNCH;

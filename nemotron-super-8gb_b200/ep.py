@@ -78,23 +78,39 @@ class ExpertParallelMoE:
         self.layout_T = layout_T
         self.ops = ops if ops is not None else CudaOps()
 
-    def forward(self, x, top_k_index, top_k_weights):
+    def forward(self, x, top_k_index, top_k_weights, marks=None):
         """x [T, 1024], top_k_index [T, k] global expert ids, top_k_weights [T, k] -> fp32 [T, 1024]:
         sum over k of weight * expert(x), the local experts' terms summed in k order on their rank and the
-        ranks' partials summed in rank order. Every rank must call with the same T and k."""
+        ranks' partials summed in rank order. Every rank must call with the same T and k.
+        marks: a list that receives (phase, CUDA event) after each phase ("start", "pack", "dispatch",
+        "experts", "return", "combine"), recorded on the current stream, for timing the exchange."""
         T, k = top_k_index.shape
         world = self.world
+
+        def mark(name):
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record()
+                marks.append((name, ev))
+
+        mark("start")
         send_x, send_meta, row_of, _ = self.ops.pack(x, top_k_index, top_k_weights, self.n_experts, world)
+        mark("pack")
         recv_x = torch.empty_like(send_x)
         recv_meta = torch.empty_like(send_meta)
         dist.all_to_all_single(recv_x, send_x, group=self.group)
         dist.all_to_all_single(recv_meta, send_meta, group=self.group)
+        mark("dispatch")
         part = self.ops.local(self.store, self.s2, recv_x.view(world * T, LAT), recv_meta.view(world * T, 2 * k),
                               self.layout_T)
         part = part.view(world, T, LAT)
+        mark("experts")
         recv_part = torch.empty_like(part)
         dist.all_to_all_single(recv_part, part, group=self.group)
-        return self.ops.combine(recv_part, row_of)
+        mark("return")
+        out = self.ops.combine(recv_part, row_of)
+        mark("combine")
+        return out
 
     __call__ = forward
 

@@ -4,9 +4,9 @@ every function computed by libqmoe_b200 (hand-written sm_100a CUDA) through its 
 
 Same names, argument order, buffer roles and return values as the reference; tensors must be CUDA
 tensors, and calls launch asynchronously on torch's current stream. Activations are not quantized
-(W4A16): codes and block scales are decoded exactly, products are exact, partial sums over each
-16-element group run in f16 after an exact power-of-two prescale of the activation and everything
-after that in fp32 (see csrc/gemv.cuh), which keeps outputs within bf16 tolerance of the fp32 path.
+(W4A16) in the decode and pair kernels: codes and block scales are decoded exactly, products are exact and
+every sum is fp32, as in the reference's kernels (qmoe_ns.py:4). moe_prefill's tensor-core GEMMs take the
+activations as three NVFP4 residual planes (rel-L2 about 5e-4 of the fp32 path, inside bf16 tolerance).
 """
 import torch
 
@@ -146,10 +146,10 @@ def moe_decode_live(slots_up, sidx, tab, s2, coef, x, h_buf, out_buf, idx_buf, c
 _PWS = {}
 
 
-def _prefill_workspace(dev, T, topk, ne):
+def _prefill_workspace(dev, T, topk, ne, layout_T):
     """Per (device, stream) workspace of qmoe_prefill_grouped, grown on demand; status word zeroed."""
     key = (dev.index, torch.cuda.current_stream(dev).cuda_stream)
-    need = int(C.lib().qmoe_prefill_workspace_bytes(T, topk, ne))
+    need = int(C.lib().qmoe_prefill_workspace_bytes(T, topk, ne, int(bool(layout_T))))
     if need == 0:
         raise C.QmoeError(f"prefill shape out of range: T={T} topk={topk} n_experts={ne}")
     ws = _PWS.get(key)
@@ -180,7 +180,7 @@ def moe_prefill(store, ids, weights, s2, X, layout_T=True, out=None):
     s2c = s2.to(torch.float32).contiguous()
     if out is None:
         out = torch.empty(T, LAT, dtype=torch.float32, device=X.device)
-    ws = _prefill_workspace(X.device, T, topk, store.shape[0])
+    ws = _prefill_workspace(X.device, T, topk, store.shape[0], layout_T)
     C.call("qmoe_prefill_grouped", C.ptr(store), int(store.stride(0)), int(store.shape[0]), int(bool(layout_T)),
            C.ptr(ids32), C.ptr(w32), C.ptr(s2c), xp, xd, T, topk, _f32(out), C.ptr(ws), ws.numel(),
            C.stream_of(X))
@@ -199,8 +199,20 @@ def prefill_status(device=None, clear=True):
 def moe_pairs_T(slots_u8, pslot, ptok, s2p, coefp, X, h_buf, out_buf):
     """qmoe_ns.py:318-324: pairs over T-layout slots. The slots used are converted to the orig layout
     in a scratch copy (from_T) and the pairs kernels run on it, as the reference engine's prompt path
-    does (nem_super.py:324-339)."""
-    uniq, inv = torch.unique(pslot.long(), return_inverse=True)
+    does (nem_super.py:324-339). The distinct slots are found on the device with a fixed bound of
+    min(P, S) rows (a sort, a first-occurrence scan and a scatter), so nothing waits for the host; rows past
+    the distinct count repeat the smallest slot and are converted but never read."""
+    P = pslot.shape[0]
+    if P == 0:
+        return out_buf[:0]
+    n = min(P, slots_u8.shape[0])
+    srt, order = torch.sort(pslot.long())
+    first = torch.ones_like(srt, dtype=torch.bool)
+    first[1:] = srt[1:] != srt[:-1]
+    rank = torch.cumsum(first, 0) - 1                    # index of each sorted pair's slot among the distinct ones
+    uniq = srt[:1].expand(n).clone()
+    uniq.scatter_(0, rank, srt)                          # equal ranks write equal slots
+    inv = torch.empty_like(rank).scatter_(0, order, rank)
     tmp = slots_u8.index_select(0, uniq).contiguous()
     from_T_batch(tmp)
     return moe_pairs(tmp, inv.to(torch.int32).contiguous(), ptok, s2p, coefp, X, h_buf, out_buf)

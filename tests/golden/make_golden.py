@@ -1,7 +1,7 @@
 """Generate the golden vectors by running the REFERENCE's own Python functions on CPU.
 
-Run here, where the reference tree is mounted (default /root/reference, override with NSREF):
-    python tests/golden/make_golden.py
+Run where a checkout of the reference is available, naming its root in NSREF:
+    NSREF=<path to the reference checkout> python tests/golden/make_golden.py
 Writes tests/golden/golden.npz and tests/golden/golden.json. The inputs are regenerated from seeds
 by tests/golden/vectors.py, so only outputs are stored. Reference functions used:
   qmoe_ns.E2M1 (qmoe_ns.py:391), deq / block_deq (qmoe_ns.py:395-412), to_T / from_T
@@ -24,7 +24,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import vectors as V  # noqa: E402
 
-REF = os.environ.get("NSREF", "/root/reference")
+REF = os.environ.get("NSREF")
 
 
 def _load(name, path):
@@ -39,6 +39,8 @@ def sha(a):
 
 
 def main():
+    if not REF or not os.path.isfile(os.path.join(REF, "qmoe_ns.py")):
+        sys.exit("set NSREF to the root of the reference checkout (the directory holding qmoe_ns.py)")
     Q = _load("ref_qmoe_ns", os.path.join(REF, "qmoe_ns.py"))
     D = _load("ref_dense_q", os.path.join(REF, "dense_q.py"))
     out, meta = {}, {}

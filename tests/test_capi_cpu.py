@@ -87,14 +87,17 @@ def test_prefill_and_ep_argument_checks_need_no_gpu(L):
     fake = ctypes.c_void_p(4096)          # 256-byte aligned stand-in pointer (never dereferenced)
     BLK = 3096576
     T, K, NE = 8, 22, 512
-    need = lib.qmoe_prefill_workspace_bytes(T, K, NE)
+    need = lib.qmoe_prefill_workspace_bytes(T, K, NE, 0)
     assert need > 0
-    assert lib.qmoe_prefill_workspace_bytes(0, K, NE) == 0                # T out of range
-    assert lib.qmoe_prefill_workspace_bytes(T, 33, NE) == 0               # topk > 32
-    assert lib.qmoe_prefill_workspace_bytes(2 * T, K, NE) > need         # grows with T
+    assert lib.qmoe_prefill_workspace_bytes(0, K, NE, 0) == 0                # T out of range
+    assert lib.qmoe_prefill_workspace_bytes(T, 33, NE, 0) == 0               # topk > 32
+    assert lib.qmoe_prefill_workspace_bytes(2 * T, K, NE, 0) > need         # grows with T
+    need_t = lib.qmoe_prefill_workspace_bytes(T, K, NE, 1)
+    # a T-layout store adds one converted down half (1,548,288 B) per expert the prompt can use: min(NE, T*K)
+    assert need_t - need == min(NE, T * K) * 1548288
 
     def pf(store=fake, stride=BLK, ne=NE, lt=1, ids=fake, w=fake, s2=fake, x=fake, dt=1, t=T, k=K, out=fake,
-           ws=fake, wsb=need):
+           ws=fake, wsb=need_t):
         return lib.qmoe_prefill_grouped(store, stride, ne, lt, ids, w, s2, x, dt, t, k, out, ws, wsb, None)
 
     assert pf(store=None) == 5
@@ -107,7 +110,8 @@ def test_prefill_and_ep_argument_checks_need_no_gpu(L):
     assert pf(stride=BLK + 8) == 2                                       # stride not a multiple of 16
     assert pf(x=ctypes.c_void_p(4096 + 8)) == 2                          # activations not 16-byte aligned
     assert pf(ws=ctypes.c_void_p(4096 + 16)) == 2                        # workspace not 256-byte aligned
-    assert pf(wsb=need - 1) == 8                                         # workspace too small
+    assert pf(wsb=need_t - 1) == 8                                       # workspace too small
+    assert pf(lt=0, wsb=need) != 8                                       # the orig layout needs no conversion area
     if not torch.cuda.is_available():
         assert pf() == 7
 

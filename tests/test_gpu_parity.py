@@ -1,10 +1,11 @@
 """GPU parity tests: libqmoe_b200 (through the drop-in qmoe_ns / dense_q modules and the C ABI) against
 the CPU oracle (oracle/) and the reference's golden vectors (tests/golden/).
 
-Bars: bit-exact for decode tables, dequantization, layouts, live-group lists and
-top-k ids; expert and layer outputs within rel-L2 1e-2 of the fp64 oracle (the fp32-dequantized CPU
-path) and, tighter, within BF16_TOL = 2^-8 (bf16's unit roundoff), which also covers the reference's
-Triton kernels (fp32 accumulation, i.e. within 1e-6 of the oracle).
+Bars: bit-exact for decode tables, dequantization, layouts, live-neuron sets,
+live-group lists and top-k ids; expert and layer outputs within rel-L2 1e-2 of the fp64 oracle (the
+fp32-dequantized CPU path). The decode and GEMV kernels accumulate in fp32 as the reference's Triton kernels do
+(qmoe_ns.py:4, dense_q.py:8), so they are held to FP32_TOL = 1e-5 of the fp64 oracle, far inside bf16's unit
+roundoff (2^-8) that bounds the reference's kernels against each other.
 """
 import hashlib
 
@@ -19,6 +20,7 @@ pytestmark = pytest.mark.gpu
 
 REL_L2 = 1e-2
 BF16_TOL = 2.0 ** -8
+FP32_TOL = 1e-5
 DEV = "cuda"
 
 
@@ -149,7 +151,7 @@ def test_decode_up_and_live_set(Q, experts, oracle_decode):
            C.dtype_code(e["x"]), C.ptr(h), C.stream_of(h))
     y64, h64, _ = oracle_decode
     hg = h.cpu().numpy()
-    assert rel_l2(hg, h64) < BF16_TOL
+    assert rel_l2(hg, h64) < FP32_TOL
     # live sets: bit-exact (the synthetic margins are wide), and they match the drawn masks
     assert np.array_equal(hg > 0, h64 > 0)
     # the realized live set is the drawn Bernoulli mask up to the rare live row that comes out negative
@@ -189,7 +191,7 @@ def test_moe_decode_groups_parity(Q, experts, oracle_decode):
     y64, h64, yj64 = oracle_decode
     yg = y.cpu().numpy()
     err = rel_l2(yg, y64)
-    assert err < REL_L2 and err < BF16_TOL, err
+    assert err < REL_L2 and err < FP32_TOL, err
     og, oc = O.live_groups(h64.astype(np.float32))
     assert np.array_equal(b["gcnt"].cpu().numpy(), oc)
     assert np.array_equal(b["gidx"].cpu().numpy(), og)
@@ -215,7 +217,7 @@ def test_down_groups_reference_form(Q, experts, oracle_decode):
     C.call("qmoe_decode_down_groups", C.ptr(tab), C.ptr(h), C.ptr(b["gidx"]), C.ptr(b["gcnt"]), C.ptr(e["s2"]),
            C.ptr(e["coef"]), K, 2, C.ptr(part), C.stream_of(h))
     y = part.sum((0, 1)).cpu().numpy()
-    assert rel_l2(y, y64) < BF16_TOL
+    assert rel_l2(y, y64) < FP32_TOL
 
 
 def test_zero_skip_vs_full_and_controls(Q, experts, oracle_decode):
@@ -230,8 +232,8 @@ def test_zero_skip_vs_full_and_controls(Q, experts, oracle_decode):
     y_full = Q.moe_decode(e["blk"], sidx, e["s2"], e["coef"], e["x"], h, out)
     y_skip = Q.moe_decode_groups(T, sidx, tab, e["s2"], e["coef"], e["x"], b["h"], b["part"], b["gidx"], b["gcnt"])
     y64 = oracle_decode[0]
-    assert rel_l2(y_full.cpu().numpy(), y64) < BF16_TOL
-    assert rel_l2(y_skip.cpu().numpy(), y_full.cpu().numpy()) < BF16_TOL
+    assert rel_l2(y_full.cpu().numpy(), y64) < FP32_TOL
+    assert rel_l2(y_skip.cpu().numpy(), y_full.cpu().numpy()) < FP32_TOL
     y_bad = Q.moe_decode_groups(T, sidx, torch.roll(tab, 1), e["s2"], e["coef"], e["x"], b["h"], b["part"],
                                 b["gidx"], b["gcnt"])
     assert rel_l2(y_bad.cpu().numpy(), y64) > 0.1
@@ -254,14 +256,18 @@ def test_decode_golden_random_blocks(Q, golden):
     out = torch.empty(K, 1024, device=DEV)
     y = Q.moe_decode(blk, sidx, s2t, ct, xt, h, out).cpu().numpy()
     gy, gh = golden["decode_y"], golden["decode_h"]
-    assert rel_l2(y, gy) < BF16_TOL
-    assert rel_l2(h.cpu().numpy(), gh) < BF16_TOL
-    # live sets bit-exact wherever the pre-activation is not within the f16 partial-sum rounding of zero
+    assert rel_l2(y, gy) < FP32_TOL
+    assert rel_l2(h.cpu().numpy(), gh) < FP32_TOL
+    # live sets: the kernel's h > 0 equals the fp64 pre-activation's sign on every neuron. The bar excludes only
+    # pre-activations within 1e-6 of max|u| of zero (none in this case: the smallest is reported on failure),
+    # where fp32 summation order alone could decide the sign.
     hh = h.cpu().numpy()
     u = np.stack([O.deq(b[:V.O_US].reshape(2688, 512), b[V.O_US:V.O_DW].reshape(2688, 64), s2[j, 0]).astype(np.float64)
                   @ x.astype(np.float64) for j, b in enumerate(blocks)])
-    margin = np.abs(u) > 1e-3 * np.abs(u).max()
-    assert np.array_equal((hh > 0)[margin], (u > 0)[margin])
+    flips = int(((hh > 0) != (u > 0)).sum())
+    margin = np.abs(u) > 1e-6 * np.abs(u).max()
+    assert np.array_equal((hh > 0)[margin], (u > 0)[margin]), f"{flips} live-set flips"
+    assert flips == 0, f"{flips} live-set flips; smallest |u|/max|u| = {np.abs(u).min() / np.abs(u).max():.2e}"
     T = blk.clone()
     Q.to_T_batch(T)
     tab = torch.tensor([T[j].data_ptr() for j in range(K)], dtype=torch.int64, device=DEV)
@@ -269,9 +275,10 @@ def test_decode_golden_random_blocks(Q, golden):
     gcnt = torch.empty(K, dtype=torch.int32, device=DEV)
     part = torch.empty(2, K, 1024, device=DEV)
     y2 = Q.moe_decode_groups(T, sidx, tab, s2t, ct, xt, h, part, gidx, gcnt).cpu().numpy()
-    assert rel_l2(y2, gy) < BF16_TOL
-    og, oc = O.live_groups(h.cpu().numpy())   # compaction of the kernel's own h is bit-exact
-    assert np.array_equal(gidx.cpu().numpy(), og) and np.array_equal(gcnt.cpu().numpy(), oc)
+    assert rel_l2(y2, gy) < FP32_TOL
+    # the fused kernels' live-group lists equal the reference's own glue on the fp64 h (qmoe_ns.py:249-251)
+    assert np.array_equal(gidx.cpu().numpy(), golden["decode_gidx"])
+    assert np.array_equal(gcnt.cpu().numpy(), golden["decode_gcnt"])
 
 
 def test_bad_slot_index_gives_nan(Q, experts):
@@ -295,7 +302,7 @@ def test_pairs_golden(Q, golden):
     y = Q.moe_pairs(blk, torch.from_numpy(pslot).to(DEV), torch.from_numpy(ptok).to(DEV),
                     torch.from_numpy(s2p).to(DEV), torch.from_numpy(coefp).to(DEV),
                     torch.from_numpy(X).to(DEV).to(torch.bfloat16), h, out)
-    assert rel_l2(y.cpu().numpy(), golden["pairs_out"]) < BF16_TOL
+    assert rel_l2(y.cpu().numpy(), golden["pairs_out"]) < FP32_TOL
 
 
 def test_pairs_vs_step(Q, experts):
@@ -321,8 +328,8 @@ def test_pairs_vs_step(Q, experts):
     for t in range(Tn):
         ref = Q.moe_decode(e["blk"], sel[t].int().contiguous(), e["s2"][sel[t]].contiguous(), w[t].contiguous(), X[t],
                            torch.empty(8, 2688, device=DEV), torch.empty(8, 1024, device=DEV))
-        # two kernel paths (pairs GEMV vs decode up/down) associate the f16 group partials differently
-        assert rel_l2(comb[t].cpu().numpy(), ref.cpu().numpy()) < 1e-3
+        # two kernel paths (pairs GEMV vs decode up/down), both fp32: they differ only in summation order
+        assert rel_l2(comb[t].cpu().numpy(), ref.cpu().numpy()) < FP32_TOL
     # T-layout slots (qmoe_ns.moe_pairs_T) give the same pairs
     T = e["blk"].clone()
     Q.to_T_batch(T)
@@ -348,9 +355,9 @@ def test_dense_golden(D, golden, fmt, seed):
     assert np.array_equal(o32.cpu().numpy().view(np.uint32), golden[f"dense_{fmt}_w32"].view(np.uint32))
     xt = torch.from_numpy(x).to(DEV).to(torch.bfloat16)
     y = D.gemv_mb(q, xt).cpu().numpy()
-    assert rel_l2(y, golden[f"dense_{fmt}_y"]) < BF16_TOL
+    assert rel_l2(y, golden[f"dense_{fmt}_y"]) < FP32_TOL
     y1 = D.gemv(q, xt[0]).cpu().numpy()
-    assert rel_l2(y1, golden[f"dense_{fmt}_y"][0]) < BF16_TOL
+    assert rel_l2(y1, golden[f"dense_{fmt}_y"][0]) < FP32_TOL
 
 
 DENSE_SHAPES = [("fp8", 4096, 4096), ("fp8", 12288, 4096), ("fp8", 4096, 8192), ("fp8", 10304, 2688),
@@ -374,8 +381,8 @@ def test_dense_gemv_shapes(D, synth, fmt, N, K):
     ref = O.dense(fmt, q["w"].cpu().numpy(), sc_np, float(q["s"]), N, K, x.float().cpu().numpy())
     for M in (1, 2, 3, 4):
         y = D.qlinear(q, x[:M].float()).float().cpu().numpy() if M > 1 else D.gemv(q, x[0]).cpu().numpy()[None]
-        assert rel_l2(y, ref[:M]) < BF16_TOL, (M, rel_l2(y, ref[:M]))
-    # M > MB_MAX: exact dequantization + cuBLAS
+        assert rel_l2(y, ref[:M]) < FP32_TOL, (M, rel_l2(y, ref[:M]))
+    # M > MB_MAX: exact dequantization + cuBLAS (bf16 operands, as the reference's dequant + F.linear)
     y5 = D.qlinear(q, torch.cat([x, x[:1]]).to(torch.bfloat16)).float().cpu().numpy()
     assert rel_l2(y5[:4], ref) < 2e-2
 
@@ -391,7 +398,7 @@ def test_dense_lm_head_parity_sampled(D, synth):
     y = D.gemv(q, x)
     rows = torch.arange(0, N, 977, device=DEV)
     ref = O.dense("fp8", codes[rows].cpu().numpy(), None, 0.00123, len(rows), K, x.float().cpu().numpy()[None])[0]
-    assert rel_l2(y[rows].cpu().numpy(), ref) < BF16_TOL
+    assert rel_l2(y[rows].cpu().numpy(), ref) < FP32_TOL
 
 
 def test_decode_groups_large_K_two_kernel_path(Q, experts, oracle_decode):
@@ -409,7 +416,7 @@ def test_decode_groups_large_K_two_kernel_path(Q, experts, oracle_decode):
     gidx = torch.empty(K, 168, dtype=torch.int32, device=DEV)
     gcnt = torch.empty(K, dtype=torch.int32, device=DEV)
     y = Q.moe_decode_groups(T, sidx, tab3, s2, coef, e["x"], h, part, gidx, gcnt)
-    assert rel_l2(y.cpu().numpy(), oracle_decode[0]) < BF16_TOL
+    assert rel_l2(y.cpu().numpy(), oracle_decode[0]) < FP32_TOL
     og, oc = O.live_groups(h.cpu().numpy())
     assert np.array_equal(gidx.cpu().numpy(), og) and np.array_equal(gcnt.cpu().numpy(), oc)
 
@@ -433,4 +440,4 @@ def test_decode_groups_graph_capture_and_determinism(Q, experts, oracle_decode):
     st.synchronize()
     for o in outs:
         assert torch.equal(o, y0)      # bit-identical replays
-    assert rel_l2(y0.cpu().numpy(), oracle_decode[0]) < BF16_TOL
+    assert rel_l2(y0.cpu().numpy(), oracle_decode[0]) < FP32_TOL
