@@ -1,22 +1,31 @@
-"""Benchmark of the B200 routed-expert path (BASELINE metric: MoE decode us/token and HBM GB/s).
+"""Benchmark of the B200 routed-expert path (BASELINE metric: MoE decode us/token and HBM GB/s; prefill tok/s
+at 1/2/4/8 B200).
 
 Default workload: full 40-layer routed-expert decode, bs = 1, one B200. All
 40 x 512 synthetic NVFP4 experts (59 GiB, T layout) are resident in HBM; per-layer live fractions are
 spread uniformly over 1-16.5%. A step is one token: 40 layer calls of the decode-step routed-expert
-forward (up GEMV + ReLU^2, live-group compaction, live-group down GEMV, fixed-order combine), each on
-its own routed top-22 experts. The per-token inputs rotate over a 64-token stream, and one token reads
-~1.5 GB of distinct expert bytes, far more than the 126 MB L2, so no step is served from L2.
+forward (up GEMV + ReLU^2, live-group compaction, live-group down GEMV, fixed-order combine; fp32
+accumulation as the reference), each on its own routed top-22 experts. The per-token inputs rotate over a
+64-token stream, and one token reads ~1.5 GB of distinct expert bytes, far more than the 126 MB L2, so no
+step is served from L2.
 
   value : device time of K steps replayed from CUDA graphs (inputs resident in HBM), us/token.
-  e2e   : the same step through the public API with host buffers: one pinned H2D copy of the token's
-          packed inputs, the 40-layer decode graph, one D2H copy of the 40 layer outputs.
-  roofline: the up GEMV kernel (the dominant kernel), timed live with CUDA events over the timed
-          region, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  e2e   : the same step through the public API with host buffers, layer by layer as the model runs it: per
+          layer, the H2D copy of that layer's routed inputs from pinned host memory, the layer call, and the
+          D2H copy of its output (layer m+1's input depends on layer m's output in the real model).
+  roofline: the up GEMV kernel (the dominant kernel), timed live with CUDA events over the timed region,
+          against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  prefill (N = 1): BASELINE config 3, one 512-expert layer, T = 2048 (and T = 64) tokens through
+          qmoe_prefill_grouped: tokens/s, roofline, e2e, CPU baseline, clocks.
+  ep (every N): BASELINE config 4, expert parallelism over the N ranks (512 / N experts of every layer per
+          rank), 40 layers, batched decode of 64 tokens per rank and prefill of 8192 tokens per rank: tokens/s
+          over all ranks (max-over-ranks device time) and the measured share of the all-to-all exchanges.
 
---impl reference: the reference's fp32 CPU expert path (nem_super.py:342-346), as restated by the
-oracle port, on the host cores, timed on a bounded sample of layers per step.
---gpus N (torchrun): N independent replicas (bs = 1 decode does not shard); value = total tokens of
-all ranks / max-over-ranks time.
+--impl reference: the reference's fp32 CPU expert path (nem_super.py:342-346), as restated by the oracle
+port, on the host cores: each step one token of config 1's own store and token stream, all 40 layers x 22
+experts, the tokens the repo arm times.
+--gpus N (torchrun): bs = 1 decode does not shard: N independent replicas (value = total tokens of all
+ranks / max-over-ranks time); the ep sub-record is the sharded path.
 """
 import argparse
 import json
@@ -32,8 +41,8 @@ sys.path.insert(0, os.path.join(ROOT, "nemotron-super-8gb_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE decode us/token (40-layer routed-expert decode, bs=1)"
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode_up_kernel launch (K = 22) from the ncu capture
-# summarised in profiles/decode_up_kernel_config1.md
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one decode_up_kernel launch at K = 22, from a
+# single-launch ncu capture of this workload; ncu cannot run inside the timed bench, so the figure is carried here
 UP_TRAFFIC_NCU = 34082560 + 768
 N_LAYERS, NE, K = 40, 512, 22
 N_TOK = 64
@@ -52,6 +61,8 @@ def parse():
     ap.add_argument("--prefill-t", type=int, default=2048, help="prefill workload: tokens per call (config 3)")
     ap.add_argument("--prefill-layout", default="orig", choices=["orig", "T"],
                     help="prefill workload: store layout (T: the down halves are converted inside the call)")
+    ap.add_argument("--no-prefill", action="store_true", help="decode workload: skip the prefill sub-record")
+    ap.add_argument("--no-ep", action="store_true", help="decode workload: skip the expert-parallel sub-record")
     return ap.parse_args()
 
 
@@ -260,29 +271,50 @@ def host_cores():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(store, s2_host, T, L, budget_s=15.0, threads=0):
-    """Reference fp32 CPU expert path (oracle port) on a bounded sample: layers of token 0."""
+def decode_token_inputs(store, s2_host, T, tok, L, layout_T):
+    """Host copies of token `tok`'s routed experts, layer by layer: [(22 orig-layout blocks, s2 [22,2], coef [22],
+    x [1024] f32)]. T-layout blocks are converted back with the oracle's from_T (the reference's prompt path
+    converts them with from_T_fast before its fp32 CPU path, nem_super.py:324-328)."""
     import numpy as np
     from oracle import oracle as O
-    n = host_cores() if threads <= 0 else threads
-    layers = list(range(0, L, max(1, L // 8)))
-    times, used = [], []
-    t_all = time.perf_counter()
-    for m in layers:
-        ids = T["IDS"][0, m].cpu().numpy()
-        blocks = [store[m * NE + int(e)].cpu().numpy() for e in ids]
-        s2 = s2_host[m][ids]
-        coef = T["W"][0, m].cpu().numpy()
-        x = T["X"][0, m].float().cpu().numpy()
+    out = []
+    for m in range(L):
+        ids = T["IDS"][tok, m]
+        rows = store.index_select(0, m * NE + ids).cpu().numpy()
+        blocks = [O.from_T(b) for b in rows] if layout_T else list(rows)
+        out.append((blocks, np.ascontiguousarray(s2_host[m][ids.cpu().numpy()]), T["W"][tok, m].cpu().numpy(),
+                    T["X"][tok, m].float().cpu().numpy()))
+    return out
+
+
+def decode_cpu_token(layers, threads):
+    """The reference's fp32 CPU expert path (nem_super.py:342-346: block_deq, relu(U x)^2, D h, x coef, summed) as
+    restated by the oracle, over one token's layers on `threads` host threads. Returns the compute seconds (the
+    host copies of the blocks are made before, untimed)."""
+    from oracle import oracle as O
+    t = 0.0
+    for blocks, s2, coef, x in layers:
         t0 = time.perf_counter()
-        O.cpu_layer_fp32(blocks, s2, coef, x, layoutT=True, nthreads=n)
-        times.append(time.perf_counter() - t0)
-        used.append(m)
-        if time.perf_counter() - t_all > budget_s:
-            break
-    per_layer = float(np.mean(times))
-    return {"value": per_layer * L * 1e6, "unit": "us/token", "cores": n, "kind": "port",
-            "sample": f"token 0, layers {used} of {L} (T layout), mean {per_layer * 1e3:.1f} ms/layer x {L}"}
+        O.cpu_layer_fp32(blocks, s2, coef, x, layoutT=False, nthreads=threads)
+        t += time.perf_counter() - t0
+    return t
+
+
+def decode_config(L, world):
+    """The `config` of the decode line, the same for the repo arm and the reference arm."""
+    return {"workload": "config1: 40-layer routed-expert decode, bs=1, HBM-resident T-layout store", "layers": L,
+            "experts": NE, "top_k": K, "tokens_rotated": N_TOK, "l2": "inputs larger than L2 (1.5 GB/token)",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+
+def cpu_baseline(store, s2_host, T, L, tok, threads=0):
+    """The reference arm's code on one token of the timed stream (token `tok`, all layers x 22 experts)."""
+    n = host_cores() if threads <= 0 else threads
+    layers = decode_token_inputs(store, s2_host, T, tok, L, layout_T=True)
+    dt = decode_cpu_token(layers, n)
+    return {"value": round(dt * 1e6, 1), "unit": "us/token", "cores": n, "kind": "port",
+            "sample": f"token {tok} of the 64-token stream, all {L} layers x {K} routed experts "
+                      f"(the reference arm's code and inputs), {dt / L * 1e3:.1f} ms/layer"}
 
 
 def run_reference(args):
@@ -300,47 +332,36 @@ def run_reference(args):
                           "runs every expert on one GPU (see --workload prefill / decode for its paths)"}), flush=True)
         return
     import torch
-    from oracle import oracle as O
     import qmoe_synth as S
-    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
     n = host_cores()
-    # the same recipe (config 1): 4 sample layers (live fractions spread over 1-16.5%), each with 22
-    # routed experts of one token, generated once on the host; a step times one layer of the
-    # reference's fp32 CPU path, and the time is scaled to 40 layers per token.
-    g = S.seeded(123, "cpu")
-    L = N_LAYERS
-    p_l = S.layer_live_fractions(L)
-    sample_layers = [0, 13, 26, 39]
-    cases = []
-    for m in sample_layers:
-        m_hat = S.unit_dir(g, "cpu")
-        blk, s2, _ = S.expert_blocks(K, p_l[m], m_hat, g, "cpu")
-        blocksT = [O.to_T(b) for b in blk.numpy()]
-        x = S.tokens(1, m_hat, g, "cpu")[0].float().numpy()
-        coef = (torch.rand(K, generator=g) * 5).numpy().astype(np.float32)
-        cases.append((blocksT, s2.numpy(), coef, x))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    # config 1's own store and token stream, generated on the device exactly as the repo arm generates them
+    # (same seeds, same draws; the orig layout, which the reference's CPU path reads), then copied to the host
+    # token by token. The timed steps are the tokens the repo arm's timed steps replay.
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L = args.layers
+    store, s2, m_hats, routers, _ = build_store(torch, S, dev, L, seed=1000, layout_T=False)
+    T = make_tokens(torch, S, dev, store, s2, m_hats, routers, N_TOK, seed=2000)
+    s2_host = s2.cpu().numpy()
     samples = []
     t_all = time.perf_counter()
     for it in range(args.warmup + args.steps):
-        blocksT, s2, coef, x = cases[it % len(cases)]
-        t0 = time.perf_counter()
-        O.cpu_layer_fp32(blocksT, s2, coef, x, layoutT=True, nthreads=n)
-        dt = time.perf_counter() - t0
+        layers = decode_token_inputs(store, s2_host, T, it % N_TOK, L, layout_T=False)
+        dt = decode_cpu_token(layers, n)
         if it >= args.warmup:
-            samples.append(dt * L * 1e6)
-        if time.perf_counter() - t_all > 150:
+            samples.append(dt * 1e6)
+        if time.perf_counter() - t_all > 900:   # a bound on the whole run; the line reports the steps timed
             break
-    per_step_layers = 1
     v = float(np.mean(samples))
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "us/token", "n_gpus": args.gpus,
-            "steps": len(samples), "warmup": args.warmup, "ms_per_step": v / 1e3, "higher_is_better": False,
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "us/token", "n_gpus": args.gpus,
+            "steps": len(samples), "warmup": args.warmup, "ms_per_step": round(v / 1e3, 3), "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1: 40-layer routed-expert decode bs=1 (sampled layers)", "layers": L,
-                       "experts": NE, "top_k": K, "layout": "T"},
-            "cpu_baseline": {"value": v, "unit": "us/token", "cores": n, "kind": "port",
-                             "sample": f"{per_step_layers} layer (22 routed experts, layers {sample_layers} "
-                                       f"cycled) per step, x {L} layers"},
-            "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": decode_config(L, world),
+            "cpu_baseline": {"value": round(v, 1), "unit": "us/token", "cores": n, "kind": "port",
+                             "sample": f"per step one token of the 64-token stream (tokens {args.warmup} onwards, as "
+                                       f"the repo arm times), all {L} layers x {K} routed experts"},
+            "e2e": {"value": round(v, 1), "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -415,6 +436,10 @@ def run_reference_dense(args):
         us = dense_cpu_reference(weights, budget_s=120.0)
         if it >= args.warmup and all(u is not None for u in us):
             samples.append(sum(us))
+    if not samples:
+        print(json.dumps({"impl": "reference", "unavailable": "the dense CPU restatement did not finish one sweep of "
+                          "the shapes within its time budget"}), flush=True)
+        return
     v = float(np.mean(samples))
     line = {"impl": "reference", "metric": DENSE_METRIC, "value": round(v, 1), "unit": "us (sum of shapes)",
             "n_gpus": args.gpus, "steps": len(samples), "warmup": args.warmup, "ms_per_step": round(v / 1e3, 3),
@@ -597,35 +622,40 @@ def prefill_cpu_reference(block_of, s2, ids, w, X, budget_s=15.0, threads=0, max
     return res + (out.numpy(),) if return_out else res
 
 
-def run_prefill(args):
-    """BASELINE config 3: the prompt path, one MoE layer of 512 synthetic NVFP4 experts (orig layout, the one
-    the reference's moe_pairs reads, or with --prefill-layout T the T layout, whose down halves the call
-    converts first: 2 more kernels; 1.585 GB resident in HBM), T tokens drawn as in config 0 and routed
-    top-22 by the synthetic router; one step = one qmoe_prefill_grouped call: routing sort, x as NVFP4
-    planes (per token, then per pair), up GEMM + ReLU^2 (block-scaled NVFP4 tcgen05), h as NVFP4 planes,
-    down GEMM, combine - 10 kernels (routing: histogram, chunk scan, expert scan, placement). value: tokens/s from CUDA events around K calls (inputs resident in HBM); e2e: the same call
-    with the token block and routing copied from pinned host memory and the output copied back, every step.
-    roofline: the whole call against the slower of the HBM bound (weights of the experts hit + activations)
-    and the NVFP4 tensor bound (true FLOPs at 4x the measured dense bf16 rate, the FP4:bf16 ratio of the
-    tensor cores); `pipe_flop` counts the MMA work actually issued (three activation planes)."""
-    import torch
-    import qmoe_ns as Q
-    import qmoe_synth as S
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(0)
-    hbm, peak_kind = peaks()
+def tensor_peak():
+    """NVFP4 dense tensor peak (TFLOP/s) and its description: 4 x the measured sustained cuBLAS bf16 rate."""
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             tpk = json.load(f)
-        tflops = 4.0 * float(tpk.get("bf16_tflops_sustained", tpk.get("bf16_tflops")))
-        tkind = "NVFP4 dense = 4 x measured cuBLAS bf16 (sustained)"
+        return 4.0 * float(tpk.get("bf16_tflops_sustained", tpk.get("bf16_tflops"))), \
+            "NVFP4 dense = 4 x measured cuBLAS bf16 (sustained)"
     except Exception:
-        tflops, tkind = 4.0 * 1400.0, "NVFP4 dense = 4 x fallback bf16 (sustained 1.4 PF)"
-    lt = args.prefill_layout == "T"
-    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303, layout_T=lt)
+        return 4.0 * 1400.0, "NVFP4 dense = 4 x fallback bf16 (sustained 1.4 PF)"
+
+
+def prefill_record(args, T, layout_T=False, steps=None, warmup=None, cpu=True, e2e=True):
+    """BASELINE config 3: the prompt path, one MoE layer of 512 synthetic NVFP4 experts (orig layout, the one
+    the reference's moe_pairs reads, or the T layout, whose down halves the call converts first: 2 more kernels;
+    1.585 GB resident in HBM), T tokens drawn as in config 0 and routed top-22 by the synthetic router; one step =
+    one qmoe_prefill_grouped call: routing sort, x as NVFP4 planes (per token, then per pair), up GEMM + ReLU^2
+    (block-scaled NVFP4 tcgen05), h as NVFP4 planes, down GEMM, combine - 10 kernels. value: tokens/s from CUDA
+    events around K calls (inputs resident in HBM); e2e: the same call with the token block and routing copied
+    from pinned host memory and the output copied back, every step. roofline: the whole call against the slower
+    of the HBM bound (weights of the experts hit + activations) and the NVFP4 tensor bound (true FLOPs at 4x the
+    measured dense bf16 rate, the FP4:bf16 ratio of the tensor cores); `pipe_flop` counts the MMA work actually
+    issued (three activation planes). Returns the record (a dict)."""
+    import torch
+    import qmoe_ns as Q
+    import qmoe_synth as S
+    steps = args.steps if steps is None else steps
+    warmup = max(3, args.warmup if warmup is None else warmup)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    hbm, peak_kind = peaks()
+    tflops, tkind = tensor_peak()
+    store, s2, m_hats, routers, _ = build_store(torch, S, dev, 1, seed=303, layout_T=layout_T)
     s2l = s2[0].contiguous()
     g = S.seeded(404, dev)
-    T = args.prefill_t
     X = S.tokens(T, m_hats[0], g, dev)
     ids, w = S.route(X, *routers[0])
     ids = ids.to(torch.int32).contiguous()
@@ -634,8 +664,8 @@ def run_prefill(args):
     out = torch.empty(T, S.LAT, device=dev)
     st = torch.cuda.Stream()
     with torch.cuda.stream(st):
-        for _ in range(max(3, args.warmup)):
-            Q.moe_prefill(store, ids, w, s2l, X, layout_T=lt, out=out)
+        for _ in range(warmup):
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=layout_T, out=out)
         st.synchronize()
         if Q.prefill_status() != 0:
             raise RuntimeError("prefill kernels reported a device-side error")
@@ -644,38 +674,37 @@ def run_prefill(args):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(st)
-        for _ in range(args.steps):
-            Q.moe_prefill(store, ids, w, s2l, X, layout_T=lt, out=out)
+        for _ in range(steps):
+            Q.moe_prefill(store, ids, w, s2l, X, layout_T=layout_T, out=out)
         e1.record(st)
         e1.synchronize()
         clocks = clk.stop()
-        ms = e0.elapsed_time(e1) / args.steps
-        # e2e: host inputs (pinned) -> device, call, output -> host, every step
-        hx = X.cpu().pin_memory()
-        hid = ids.cpu().pin_memory()
-        hw = w.cpu().pin_memory()
-        hout = torch.empty(T, S.LAT, dtype=torch.float32).pin_memory()
-        dx, did, dw = torch.empty_like(X), torch.empty_like(ids), torch.empty_like(w)
-        ee = max(5, args.steps // 2)
-        e2 = torch.cuda.Event(enable_timing=True)
-        e3 = torch.cuda.Event(enable_timing=True)
-        e2.record(st)
-        for _ in range(ee):
-            dx.copy_(hx, non_blocking=True)
-            did.copy_(hid, non_blocking=True)
-            dw.copy_(hw, non_blocking=True)
-            Q.moe_prefill(store, did, dw, s2l, dx, layout_T=lt, out=out)
-            hout.copy_(out, non_blocking=True)
-        e3.record(st)
-        e3.synchronize()
-        ms_e2e = e2.elapsed_time(e3) / ee
+        ms = e0.elapsed_time(e1) / steps
+        ms_e2e, ee = None, max(5, steps // 2)
+        if e2e:   # host inputs (pinned) -> device, call, output -> host, every step
+            hx = X.cpu().pin_memory()
+            hid = ids.cpu().pin_memory()
+            hw = w.cpu().pin_memory()
+            hout = torch.empty(T, S.LAT, dtype=torch.float32).pin_memory()
+            dx, did, dw = torch.empty_like(X), torch.empty_like(ids), torch.empty_like(w)
+            e2 = torch.cuda.Event(enable_timing=True)
+            e3 = torch.cuda.Event(enable_timing=True)
+            e2.record(st)
+            for _ in range(ee):
+                dx.copy_(hx, non_blocking=True)
+                did.copy_(hid, non_blocking=True)
+                dw.copy_(hw, non_blocking=True)
+                Q.moe_prefill(store, did, dw, s2l, dx, layout_T=layout_T, out=out)
+                hout.copy_(out, non_blocking=True)
+            e3.record(st)
+            e3.synchronize()
+            ms_e2e = e2.elapsed_time(e3) / ee
     flop = T * K * PREFILL_FLOP_PER_PAIR
     wbytes = uniq * S.BLOCK
     act_bytes = T * S.LAT * 2 + T * S.LAT * 4 + T * K * 8
     t_hbm = (wbytes + act_bytes) / (hbm * 1e6)      # ms
     t_tc = flop / (tflops * 1e9)                    # ms
-    bound = "hbm" if t_hbm >= t_tc else "tensor"
-    if bound == "hbm":
+    if t_hbm >= t_tc:
         roof = {"bound": "hbm", "achieved": round((wbytes + act_bytes) / ms / 1e6, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(t_hbm / ms, 4), "peak_kind": f"{peak_kind} (HBM copy)"}
     else:
@@ -685,58 +714,76 @@ def run_prefill(args):
     roof["algorithmic"] = {"flop": flop, "weight_bytes": wbytes, "activation_bytes": act_bytes,
                            "t_hbm_ms": round(t_hbm, 4), "t_tensor_ms": round(t_tc, 4),
                            "pipe_flop": 3 * flop, "pipe_tflops": round(3 * flop / ms / 1e9, 1)}
-    line = {"metric": PREFILL_METRIC, "value": round(T / ms * 1e3, 1),
-            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
-            "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
-            "data": "synthetic",
-            "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
-                       "unique_experts": uniq, "layout": args.prefill_layout, "l2": "weights (1.585 GB) exceed L2"},
-            "roofline": roof, "clocks": clocks,
-            "e2e": {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
-                    "d2h_bytes_per_step": int(out.numel() * 4)},
-            "gpu_launches": (12 if lt else 10) * args.steps}
-    if not args.no_cpu_baseline:
+    rec = {"metric": PREFILL_METRIC, "value": round(T / ms * 1e3, 1), "unit": "tokens/s", "steps": steps,
+           "warmup": warmup, "ms_per_step": round(ms, 5),
+           "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
+           "config": {"workload": f"config3: prefill T={T}", "T": T, "top_k": K, "experts": NE,
+                      "unique_experts": uniq, "layout": "T" if layout_T else "orig",
+                      "l2": "weights (1.585 GB) exceed L2"},
+           "roofline": roof, "clocks": clocks, "gpu_launches": (12 if layout_T else 10) * steps}
+    if ms_e2e is not None:
+        rec["e2e"] = {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
+                      "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
+                      "d2h_bytes_per_step": int(out.numel() * 4)}
+    if cpu and not args.no_cpu_baseline:
         from oracle import oracle as O
         sh = s2l.cpu().numpy()
 
         def block_of(e):   # the orig-layout block (the reference's prompt path converts T blocks first)
             b = store[e].cpu().numpy()
-            return O.from_T(b) if lt else b
+            return O.from_T(b) if layout_T else b
         v, n, sample = prefill_cpu_reference(block_of, sh, ids.cpu().numpy(), w.cpu().numpy(),
-                                             X.float().cpu().numpy())
-        line["cpu_baseline"] = {"value": round(v, 1), "unit": "tokens/s", "cores": n, "kind": "port",
-                                "sample": sample}
+                                             X.float().cpu().numpy(), budget_s=10.0)
+        rec["cpu_baseline"] = {"value": round(v, 1), "unit": "tokens/s", "cores": n, "kind": "port", "sample": sample}
+    del store
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_prefill(args):
+    """--workload prefill: the prefill record of --prefill-t tokens as the line."""
+    rec = prefill_record(args, args.prefill_t, layout_T=args.prefill_layout == "T")
+    line = dict(rec)
+    line.update({"n_gpus": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "data": "synthetic"})
     print(json.dumps(line), flush=True)
 
 
-def run_ep(args):
-    """BASELINE config 4: expert parallelism. The 512 experts of every layer are sharded over the N ranks
-    (expert e on rank e // (512 / N), orig layout, resident in HBM); each rank holds a batch of --ep-t tokens.
-    A step = `--layers` MoE layers, each an ExpertParallelMoE forward: dispatch pack, NCCL all_to_all of the
-    token blocks and routing, the local experts (block-scaled NVFP4 tcgen05 grouped GEMM), all_to_all of
-    the partial outputs,
-    rank-order combine. value = tokens of all ranks per second of max-over-ranks device time."""
+def ep_init(world, rank, local):
+    """The process group for expert parallelism (NCCL; a one-rank group when not launched by torchrun)."""
     import datetime
+    import torch
+    import torch.distributed as dist
+    dev = torch.device("cuda", local)
+    if not dist.is_initialized():
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29533")
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    return dev
+
+
+EP_PHASES = ("pack", "dispatch", "experts", "return", "combine")
+
+
+def ep_record(args, world, rank, local, batches=((64, "decode_batch"), (8192, "prefill")), layers=None):
+    """BASELINE config 4: expert parallelism. The 512 experts of every layer are sharded over the N ranks
+    (expert e on rank e // (512 / N), orig layout, resident in HBM); each rank holds a batch of T tokens per
+    layer. A step = `layers` MoE layers, each an ExpertParallelMoE forward: dispatch pack, NCCL all_to_all of the
+    token blocks and routing, the local experts (block-scaled NVFP4 tcgen05 grouped GEMM), all_to_all of the
+    partial outputs, rank-order combine. Per batch size: value = tokens of all ranks per second of max-over-ranks
+    device time; `phases` = the per-step time of each phase, measured with CUDA events around the phases over one
+    extra step (max over ranks), and `a2a_share` = the two exchanges' share of it. Every rank takes the same
+    collective steps. Returns the record on rank 0 (None elsewhere)."""
     import torch
     import torch.distributed as dist
     import ep as EP
     import qmoe_ns as Q
     import qmoe_synth as S
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world == 1:
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29533")
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                            device_id=dev)
-    L, T = args.layers, args.ep_t
+    dev = ep_init(world, rank, local)
+    L = args.layers if layers is None else layers
     el = NE // world
-    g = S.seeded(1234, dev)
+    g = S.seeded(1234 + rank, dev)
     # this rank's experts of every layer (generated on the device, orig layout)
     store = torch.empty(L * el, S.BLOCK, dtype=torch.uint8, device=dev)
     s2 = torch.empty(L, el, 2, dtype=torch.float32, device=dev)
@@ -752,78 +799,112 @@ def run_ep(args):
             store[m * el + e0:m * el + e0 + nb].copy_(blk)
             s2[m, e0:e0 + nb] = s2b
             del blk
-    layers = [EP.ExpertParallelMoE(store[m * el:(m + 1) * el], s2[m], n_experts=NE, layout_T=False)
-              for m in range(L)]
-    gx = S.seeded(555 + rank, dev)
-    X = [S.tokens(T, m_hats[m], gx, dev) for m in range(L)]
-    R = [S.route(X[m], *routers[m]) for m in range(L)]
+    moe = [EP.ExpertParallelMoE(store[m * el:(m + 1) * el], s2[m], n_experts=NE, layout_T=False) for m in range(L)]
+    out = {"config": {"workload": f"config4: EP{world}, {L} layers", "layers": L, "experts_per_rank": el,
+                      "parallelism": f"ep{world}", "exchange": "NCCL all_to_all, fixed T-row blocks"}}
+    clocks = None
+    for T, name in batches:
+        steps = max(3, min(args.steps, 10 if T > 1024 else args.steps))
+        warmup = 3
+        gx = S.seeded(555 + rank, dev)
+        X = [S.tokens(T, m_hats[m], gx, dev) for m in range(L)]
+        R = [S.route(X[m], *routers[m]) for m in range(L)]
 
-    def step():
-        outs = []
-        for m in range(L):
-            outs.append(layers[m](X[m], R[m][0], R[m][1]))
-        return outs
+        def step(marks=None):
+            for m in range(L):
+                moe[m](X[m], R[m][0], R[m][1], marks=marks)
 
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    if Q.prefill_status() != 0:
-        raise RuntimeError("expert kernels reported a device-side error")
-    clk = Clocks(local)
-    if rank == 0:
-        clk.start()
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    e1.synchronize()
-    dist.barrier()
-    torch.cuda.synchronize()
-    clocks = clk.stop() if rank == 0 else None
-    ms = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms.item())
-    # e2e through the public module: host token blocks + routing in, host outputs back, every step
-    hX = [x.cpu().pin_memory() for x in X]
-    hI = [r[0].cpu().pin_memory() for r in R]
-    hW = [r[1].cpu().pin_memory() for r in R]
-    hO = torch.empty(L, T, S.LAT, dtype=torch.float32).pin_memory()
-    ee = max(3, args.steps // 2)
-    dist.barrier()
-    torch.cuda.synchronize()
-    e2 = torch.cuda.Event(enable_timing=True)
-    e3 = torch.cuda.Event(enable_timing=True)
-    e2.record()
-    for _ in range(ee):
-        for m in range(L):
-            y = layers[m](hX[m].to(dev, non_blocking=True), hI[m].to(dev, non_blocking=True), hW[m].to(dev, non_blocking=True))
-            hO[m].copy_(y, non_blocking=True)
-    e3.record()
-    e3.synchronize()
-    me = torch.tensor([e2.elapsed_time(e3) / ee], device=dev)
-    dist.all_reduce(me, op=dist.ReduceOp.MAX)
-    me = float(me.item())
-    if rank == 0:
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize()
+        if Q.prefill_status() != 0:
+            raise RuntimeError("expert kernels reported a device-side error")
+        clk = Clocks(local)
+        if rank == 0:
+            clk.start()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        e1.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        c = clk.stop() if rank == 0 else None
+        clocks = clocks or c
+        ms = torch.tensor([e0.elapsed_time(e1) / steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        # one more step with events between the phases of every layer
+        marks = []
+        step(marks)
+        torch.cuda.synchronize()
+        ph = {p: 0.0 for p in EP_PHASES}
+        for i in range(len(marks)):
+            name_i, ev = marks[i]
+            if name_i in ph:
+                ph[name_i] += marks[i - 1][1].elapsed_time(ev)
+        pt = torch.tensor([ph[p] for p in EP_PHASES], device=dev)
+        dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        ph = {p: round(float(v), 4) for p, v in zip(EP_PHASES, pt.tolist())}
+        tot = sum(ph.values())
+        # e2e through the public module: host token blocks + routing in, host outputs back, every layer
+        hX = [x.cpu().pin_memory() for x in X]
+        hI = [r[0].cpu().pin_memory() for r in R]
+        hW = [r[1].cpu().pin_memory() for r in R]
+        hO = torch.empty(L, T, S.LAT, dtype=torch.float32).pin_memory()
+        ee = max(2, steps // 2)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e2 = torch.cuda.Event(enable_timing=True)
+        e3 = torch.cuda.Event(enable_timing=True)
+        e2.record()
+        for _ in range(ee):
+            for m in range(L):
+                y = moe[m](hX[m].to(dev, non_blocking=True), hI[m].to(dev, non_blocking=True),
+                           hW[m].to(dev, non_blocking=True))
+                hO[m].copy_(y, non_blocking=True)
+        e3.record()
+        e3.synchronize()
+        me = torch.tensor([e2.elapsed_time(e3) / ee], device=dev)
+        dist.all_reduce(me, op=dist.ReduceOp.MAX)
+        me = float(me.item())
         toks = T * world
-        line = {"metric": "MoE expert-parallel tokens/s (40-layer routed experts, top-22 of 512)",
-                "value": round(toks / ms * 1e3, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-                "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5), "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
-                "data": "synthetic",
-                "config": {"workload": f"config4: EP{world}, {T} tokens per rank, {L} layers", "layers": L,
-                           "tokens_per_rank": T, "experts_per_rank": el, "parallelism": f"ep{world}",
-                           "exchange": "NCCL all_to_all, fixed T-row blocks"},
-                "clocks": clocks,
-                "e2e": {"value": round(toks / me * 1e3, 1), "unit": "tokens/s",
-                        "h2d_bytes_per_step": int(L * T * (S.LAT * 2 + K * 12)),
-                        "d2h_bytes_per_step": int(L * T * S.LAT * 4)},
-                "gpu_launches": L * args.steps * (2 + 10 + 1)}
-        print(json.dumps(line), flush=True)
+        out[name] = {"tokens_per_rank": T, "value": round(toks / ms * 1e3, 1), "unit": "tokens/s",
+                     "ms_per_step": round(ms, 4), "steps": steps, "warmup": warmup,
+                     "phases_ms_per_step": ph, "a2a_share": round((ph["dispatch"] + ph["return"]) / tot, 4) if tot else None,
+                     "e2e": {"value": round(toks / me * 1e3, 1), "unit": "tokens/s",
+                             "h2d_bytes_per_step": int(L * T * (S.LAT * 2 + K * 12)),
+                             "d2h_bytes_per_step": int(L * T * S.LAT * 4)},
+                     "gpu_launches": L * steps * (2 + 10 + 1)}
+        del X, R, hX, hI, hW, hO
+    out["clocks"] = clocks
+    del moe, store
+    torch.cuda.empty_cache()
     dist.barrier()
+    return out if rank == 0 else None
+
+
+def run_ep(args):
+    """--workload ep: the expert-parallel record of --ep-t tokens per rank as the line."""
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    rec = ep_record(args, world, rank, local, batches=((args.ep_t, "batch"),))
+    if rank == 0:
+        b = rec["batch"]
+        line = {"metric": "MoE expert-parallel tokens/s (40-layer routed experts, top-22 of 512)", "value": b["value"],
+                "unit": "tokens/s", "n_gpus": world, "steps": b["steps"], "warmup": b["warmup"],
+                "ms_per_step": b["ms_per_step"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "nvfp4 weights x 3 nvfp4 activation planes -> f32 (tcgen05 kind::mxf4nvf4 block16)",
+                "data": "synthetic", "config": dict(rec["config"], tokens_per_rank=args.ep_t),
+                "clocks": rec["clocks"], "e2e": b["e2e"], "gpu_launches": b["gpu_launches"],
+                "phases_ms_per_step": b["phases_ms_per_step"], "a2a_share": b["a2a_share"]}
+        print(json.dumps(line), flush=True)
     dist.destroy_process_group()
 
 
@@ -941,34 +1022,68 @@ def main():
     hbm, peak_kind = peaks()
     up_gbs = up_bytes / (up_us * 1e-6) / 1e9
 
-    # ---- e2e through the public path with host buffers
-    pin_in = {k: T[k].cpu().pin_memory() for k in ("X", "SIDX", "TAB", "S2", "W")}
-    st_in = {k: torch.empty_like(T[k][0]) for k in pin_in}
-    y_host = torch.empty(L, S.LAT, dtype=torch.float32).pin_memory()
-    g_e2e = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g_e2e, stream=stream):
-        step.launch(st_in["X"], st_in["SIDX"], st_in["TAB"], st_in["S2"], st_in["W"], stream.cuda_stream)
-    h2d = sum(pin_in[k][0].numel() * pin_in[k][0].element_size() for k in pin_in)
-    d2h = y_host.numel() * 4
+    # ---- e2e through the public path with host buffers, layer by layer as the model runs it: per layer one H2D
+    # copy of that layer's packed routed inputs (x, slot ids, block addresses, s2, weights) from pinned host memory,
+    # the layer's qmoe_decode_groups call, and one D2H copy of its output y, each layer after the previous one's
+    # output is back (layer m+1's input depends on layer m's output). The 40-layer sequence is one CUDA graph; two
+    # pinned staging records alternate, each refilled on the host for the next token once its last replay is done.
+    REC = 2048 + K * (4 + 8 + 8 + 4)   # x bf16 | sidx i32 | tab i64 | s2 f32 x2 | coef f32
+    offs = {"X": 0, "SIDX": 2048, "TAB": 2048 + 4 * K, "S2": 2048 + 12 * K, "W": 2048 + 20 * K}
+    host_all = torch.empty(N_TOK, L, REC, dtype=torch.uint8)
+    for k_, o_ in offs.items():
+        src = T[k_].cpu().contiguous().view(torch.uint8).reshape(N_TOK, L, -1)
+        host_all[:, :, o_:o_ + src.shape[2]] = src
+    stage = [torch.empty(L, REC, dtype=torch.uint8).pin_memory() for _ in range(2)]
+    rec_dev = torch.empty(L, REC, dtype=torch.uint8, device=dev)
+    y_host = [torch.empty(L, S.LAT, dtype=torch.float32).pin_memory() for _ in range(2)]
+
+    def view(k_, m, dt, n):
+        return rec_dev[m, offs[k_]:offs[k_] + n * torch.tensor([], dtype=dt).element_size()].view(dt)
+
+    fn = C.lib().qmoe_decode_groups
+    g_e2e = []
+    for b in range(2):
+        stage[b].copy_(host_all[0])
+        gph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gph, stream=stream):
+            for m in range(L):
+                rec_dev[m].copy_(stage[b][m], non_blocking=True)
+                rc = fn(store.data_ptr(), store.stride(0), store.shape[0], view("SIDX", m, torch.int32, K).data_ptr(),
+                        view("TAB", m, torch.int64, K).data_ptr(), view("S2", m, torch.float32, 2 * K).data_ptr(),
+                        view("W", m, torch.float32, K).data_ptr(), view("X", m, torch.bfloat16, S.LAT).data_ptr(), 1, K,
+                        step.h[m].data_ptr(), step.gidx[m].data_ptr(), step.gcnt[m].data_ptr(), step.part[m].data_ptr(),
+                        step.Y[m].data_ptr(), step.ws.data_ptr(), step.ws.numel(), stream.cuda_stream)
+                assert rc == 0
+                y_host[b][m].copy_(step.Y[m], non_blocking=True)
+        g_e2e.append(gph)
+    done = [torch.cuda.Event(), torch.cuda.Event()]
+    h2d = L * REC
+    d2h = L * S.LAT * 4
     e_steps = max(20, args.steps // 2)
+
+    def e2e_run(n, first):
+        for i in range(n):
+            b = i & 1
+            done[b].synchronize()               # this staging record's last replay has finished reading it
+            stage[b].copy_(host_all[(first + i) % N_TOK])
+            g_e2e[b].replay()
+            done[b].record(stream)
+
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            for k in pin_in:
-                st_in[k].copy_(pin_in[k][i % N_TOK], non_blocking=True)
-            g_e2e.replay()
-            y_host.copy_(step.Y, non_blocking=True)
+        e2e_run(args.warmup, 0)
         stream.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(stream)
-        for i in range(e_steps):
-            for k in pin_in:
-                st_in[k].copy_(pin_in[k][i % N_TOK], non_blocking=True)
-            g_e2e.replay()
-            y_host.copy_(step.Y, non_blocking=True)
+        e2e_run(e_steps, args.warmup)
         e1.record(stream)
         e1.synchronize()
     e2e_ms = e0.elapsed_time(e1)
+    # the last token's outputs came back and equal the device-resident path's for the same token
+    ref_tok = (args.warmup + e_steps - 1) % N_TOK
+    graphs[ref_tok].replay()
+    torch.cuda.synchronize()
+    e2e_ok = bool(torch.equal(y_host[(e_steps - 1) & 1], step.Y.cpu()))
     t_e2e = torch.tensor([e2e_ms], device=dev)
     if world > 1:
         dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
@@ -977,8 +1092,9 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         s2_host = s2.cpu().numpy()
-        cpu = cpu_baseline(store, s2_host, T, L)
+        cpu = cpu_baseline(store, s2_host, T, L, tok=args.warmup % N_TOK)
 
+    line = None
     if rank == 0:
         step_gbs = bytes_per_token / (us_per_token_rank * 1e-6) / 1e9
         line = {
@@ -986,26 +1102,40 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4xbf16->f32",
             "data": "synthetic",
-            "config": {"workload": "config1: 40-layer routed-expert decode, bs=1, HBM-resident T-layout store",
-                       "layers": L, "experts": NE, "top_k": K, "tokens_rotated": N_TOK,
-                       "live_fraction": round(live_frac, 4), "l2": "inputs larger than L2 (1.5 GB/token)",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "config": decode_config(L, world),
+            "live_fraction": round(live_frac, 4),
             "hbm_gbs_step": round(step_gbs, 1), "hbm_frac_step": round(step_gbs / hbm, 4),
             "bytes_per_token": int(bytes_per_token),
             "roofline": {"kernel": "decode_up_kernel", "bound": "hbm", "achieved": round(up_gbs, 1), "peak": hbm,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / hbm, 4),
-                         "traffic": UP_TRAFFIC_NCU, "traffic_source": "profiles/decode_up_kernel_config1.md",
+                         "traffic": UP_TRAFFIC_NCU,
+                         "traffic_source": "ncu single-launch capture of this kernel at K=22 (DRAM read + write)",
                          "bytes_per_launch": up_bytes, "us_per_launch": round(up_us, 3)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/token", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h)},
+                    "d2h_bytes_per_step": int(d2h), "copies": "per layer: one H2D of its inputs, one D2H of y",
+                    "matches_device_path": e2e_ok},
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
             "build_s": round(t_build, 1),
         }
+    del graphs, g_e2e, up_graphs, step, store, T
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+    # ---- sub-records: prefill (config 3, one GPU) and expert parallelism (config 4, every N)
+    if world == 1 and not args.no_prefill:
+        pre = prefill_record(args, 2048, steps=max(10, args.steps))
+        pre["t64"] = prefill_record(args, 64, steps=max(10, args.steps), cpu=False, e2e=False)
+        pre["t64"] = {k_: pre["t64"][k_] for k_ in ("value", "unit", "ms_per_step", "roofline")}
+        line["prefill"] = pre
+    if not args.no_ep:
+        rec = ep_record(args, world, rank, local)
+        if rank == 0:
+            line["ep"] = rec
+    if rank == 0:
         print(json.dumps(line), flush=True)
-    del graphs, g_e2e
-    if world > 1:
+    if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
 

@@ -100,3 +100,28 @@ def test_dense_and_ep_reference_arms():
     assert line["metric"] == bench.DENSE_METRIC and line["higher_is_better"] is False and line["value"] > 0
     ep = json.loads(_run("--impl", "reference", "--workload", "ep", "--steps", "1", "--warmup", "0").strip())
     assert ep["impl"] == "reference" and "unavailable" in ep
+
+
+def test_decode_reference_path_matches_oracle(monkeypatch):
+    """The decode reference arm's code (decode_token_inputs + decode_cpu_token: the reference's fp32 CPU expert
+    path per layer) on a tiny store: both layouts give the same host blocks, and each layer's fp32 result is
+    within 1e-5 of the fp64 oracle."""
+    monkeypatch.setattr(bench, "NE", 4)
+    g = S.seeded(3, "cpu")
+    m_hat = S.unit_dir(g, "cpu")
+    L, k = 2, 3
+    blk, s2, _ = S.expert_blocks(L * 4, 0.1, m_hat, g, "cpu")
+    storeT = torch.from_numpy(np.stack([O.to_T(b) for b in blk.numpy()]))
+    T = {"IDS": torch.tensor([[[0, 2, 3], [1, 2, 0]]]), "W": torch.rand(1, L, k, generator=g),
+         "X": S.tokens(L, m_hat, g, "cpu").view(1, L, 1024)}
+    s2h = s2.view(L, 4, 2).numpy()
+    layers = bench.decode_token_inputs(blk, s2h, T, 0, L, layout_T=False)
+    layersT = bench.decode_token_inputs(storeT, s2h, T, 0, L, layout_T=True)
+    for (b0, *_), (b1, *_) in zip(layers, layersT):
+        assert all(np.array_equal(a, b) for a, b in zip(b0, b1))
+    assert bench.decode_cpu_token(layers, 2) > 0
+    for blocks, s2m, coef, x in layers:
+        y32 = O.cpu_layer_fp32(blocks, s2m, coef, x, nthreads=2)
+        y64, _, _ = O.moe_decode(blocks, s2m, coef, x)
+        assert np.linalg.norm(y32 - y64) / np.linalg.norm(y64) < 1e-5
+    assert bench.decode_config(40, 1) == bench.decode_config(40, 1) and "parallelism" in bench.decode_config(40, 2)
