@@ -421,6 +421,31 @@ def test_decode_groups_large_K_two_kernel_path(Q, experts, oracle_decode):
     assert np.array_equal(gidx.cpu().numpy(), og) and np.array_equal(gcnt.cpu().numpy(), oc)
 
 
+@pytest.mark.parametrize("K", [1, 4, 8, 9, 31, 32, 33])
+def test_decode_groups_K_range(Q, experts, K):
+    """moe_decode_groups for K experts (entry j -> expert j mod 22): K <= 32 takes the cluster form of the down
+    kernel (CTAs of 1-4 experts, empty CTAs when K < 8), K = 33 the arrival-counter form; y within 1e-5 of the
+    fp64 oracle, gidx / gcnt the exact compaction of the kernel's h."""
+    e = experts
+    T, tab, _ = _T_setup(Q, e)
+    idx = torch.arange(K, device=DEV) % 22
+    coef = (torch.rand(K, generator=torch.Generator(device=DEV).manual_seed(K), device=DEV) + 0.1).contiguous()
+    h = torch.empty(K, Q.INTER, device=DEV)
+    part = torch.empty(2, K, Q.LAT, device=DEV)
+    gidx = torch.empty(K, 168, dtype=torch.int32, device=DEV)
+    gcnt = torch.empty(K, dtype=torch.int32, device=DEV)
+    y = Q.moe_decode_groups(T, idx.to(torch.int32).contiguous(), tab[idx].contiguous(), e["s2"][idx].contiguous(), coef,
+                            e["x"], h, part, gidx, gcnt)
+    torch.cuda.synchronize()
+    assert Q.decode_groups_status() == 0
+    ii = idx.cpu().numpy()
+    y64, _, yj64 = O.moe_decode([e["blk_np"][i] for i in ii], e["s2_np"][ii], coef.cpu().numpy(), e["x_np"])
+    assert rel_l2(y.cpu().numpy(), y64) < FP32_TOL
+    assert rel_l2(part[0].cpu().numpy(), yj64) < FP32_TOL
+    og, oc = O.live_groups(h.cpu().numpy())
+    assert np.array_equal(gidx.cpu().numpy(), og) and np.array_equal(gcnt.cpu().numpy(), oc)
+
+
 def test_decode_groups_graph_capture_and_determinism(Q, experts, oracle_decode):
     e = experts
     K = 22
