@@ -94,16 +94,13 @@ __device__ __forceinline__ float up_row(const uint4 w, uint16_t sc, const UpX<XF
     return (g[0][0] + g[0][1]) * sf.x + (g[1][0] + g[1][1]) * sf.y;
 }
 
-// One 8-row tile of `_up` (qmoe_ns.py:24-44) from a lane's share of its codes and scales: per row the lane's two
-// 16-element groups in fp32 (as the reference accumulates), a 9-shuffle butterfly over the 8 rows, then ReLU^2,
-// h, the tile's 8-bit live-neuron mask and the L2 prefetch of the live neurons' down rows.
+// The 8 row dot products of a tile: each lane's two fp32 group partials per row, reduced over the warp by a
+// 9-shuffle butterfly; lanes 4r .. 4r+3 return row r (unscaled).
 template <bool XF32>
-__device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int j, int hg, float mult, bool bad,
-                                        const UpX<XF32> &x, int lane, const uint8_t *const *s_tab) {
+__device__ __forceinline__ float up_tile_dot(const UpTile &cur, const UpX<XF32> &x, int lane) {
     float part[UP_ROWS];
 #pragma unroll
     for (int r = 0; r < UP_ROWS; ++r) part[r] = up_row<XF32>(cur.w[r], cur.sc[r], x);
-    // butterfly: 8 row partials over 32 lanes -> lanes 4r..4r+3 hold row r
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const bool up = lane & 16;
@@ -123,8 +120,16 @@ __device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int 
     }
     part[0] += __shfl_xor_sync(0xffffffffu, part[0], 2);
     part[0] += __shfl_xor_sync(0xffffffffu, part[0], 1);
+    return part[0];
+}
 
-    const float u = fmaxf(part[0] * mult, 0.f);   // ReLU^2 (qmoe_ns.py:42-44)
+// One 8-row tile of `_up` (qmoe_ns.py:24-44) from a lane's share of its codes and scales: per row the lane's two
+// 16-element groups in fp32 (as the reference accumulates), a 9-shuffle butterfly over the 8 rows, then ReLU^2,
+// h, the tile's 8-bit live-neuron mask and the L2 prefetch of the live neurons' down rows.
+template <bool XF32>
+__device__ __forceinline__ void up_tile(const UpArgs &a, const UpTile &cur, int j, int hg, float mult, bool bad,
+                                        const UpX<XF32> &x, int lane, const uint8_t *const *s_tab) {
+    const float u = fmaxf(up_tile_dot<XF32>(cur, x, lane) * mult, 0.f);   // ReLU^2 (qmoe_ns.py:42-44)
     float hv = u * u;
     if (bad) hv = __int_as_float(0x7fc00000);
     const bool lead = (lane & 3) == 0;
@@ -515,6 +520,16 @@ __device__ __forceinline__ void st_cluster_f32(float *local, uint32_t rank, floa
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
 }
 
+// Split cluster barrier at kernel entry: every CTA arrives at once and waits just before its first access to another
+// CTA's shared memory, which must not happen before all CTAs of the cluster have started.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void cluster_arrive_release() {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
@@ -543,6 +558,7 @@ __global__ void __launch_bounds__(DC_TPE * DC_MAXE) decode_down_cluster_kernel(D
     const uint8_t *blk = has ? reinterpret_cast<const uint8_t *>(a.tab[j]) : nullptr;
     const bool bad = has && ((reinterpret_cast<uintptr_t>(blk) & 15u) != 0 || blk == nullptr);
     const float cmul = has ? a.coef[j] * a.s2[2 * j + 1] : 0.f;
+    cluster_arrive_relaxed();
 
     pdl_launch_dependents();   // the next kernel (the next layer's up) may start its launch now
     pdl_wait();                // the up kernel's h and masks are complete and visible
@@ -681,6 +697,7 @@ __global__ void __launch_bounds__(DC_TPE * DC_MAXE) decode_down_cluster_kernel(D
     // CTAs in rank order. Only rank 0 waits: the others have nothing left to do and exit (a cluster-barrier wait
     // counts only threads that have not exited), while rank 0, the only CTA whose shared memory is written
     // remotely, stays until it has read it.
+    cluster_wait();   // every CTA of the cluster has started
     if (tid < DC_ROWS) {
         float v = 0.f;
         for (int e = 0; e < nexp && c + DC_CL * e < a.K; ++e) v += pe[e][tid];
@@ -695,6 +712,306 @@ __global__ void __launch_bounds__(DC_TPE * DC_MAXE) decode_down_cluster_kernel(D
             for (int r = 0; r < DC_CL; ++r) v += gather[r][tid];
             a.y[rc * DC_ROWS + tid] = v;
         }
+    }
+}
+
+// ------------------------------------------------------------------ the decode-step layer fused per CTA
+// `moe_decode_groups` (qmoe_ns.py:245-255) with each expert's neurons split over a cluster of S CTAs (S*K <= SMs):
+// CTA s of expert j owns neurons [s*2688/S, (s+1)*2688/S). It streams their up rows (`_up`, qmoe_ns.py:24-44, the
+// tiles of decode_up_kernel with the next tile's loads in flight), keeps h and the live masks in shared memory
+// (and writes h out), lists its live neurons, and at once adds their down contributions (`_down_groups`,
+// qmoe_ns.py:209-239, over the T layout: a neuron's 512-byte row of dnT_w covers all 1024 output rows): warp w
+// takes live neurons w, w+12, ..., lane l the rows 32l .. 32l+31, fp32 accumulation of (e2m1 * e4m3, exact in f16)
+// * h. So no CTA waits for another's up tiles, and the down work of early CTAs overlaps the up tail of late ones.
+// The CTA's 1024 partial sums (its 12 warps in order) and its groups' live flags go to cluster rank 0's shared
+// memory; rank 0 sums the S CTAs in rank order into part[j] (x coef_j * s2d_j) and writes gidx / gcnt for the
+// expert. decode_finish_kernel, a programmatic dependent, sums the experts in slot order into y.
+constexpr int FL_NW = UP_NW;                   // 12 warps, as the up kernel
+constexpr int FL_THREADS = 32 * FL_NW;
+constexpr int FL_MAXS = 8;                     // CTAs per expert (portable cluster size)
+constexpr int FL_NB = 4;                       // live neurons per warp with all loads in flight at once
+// dynamic shared memory of the fused layer kernel (byte offsets)
+constexpr int FL_OFF_H = 0;                                   // h of the CTA's neurons, f32 [<= 2688]
+constexpr int FL_OFF_NL = FL_OFF_H + INTER * 4;               // live neurons (CTA-local index), u16 [<= 2688]
+constexpr int FL_OFF_MASK = FL_OFF_NL + INTER * 2;            // live mask per 8-row tile, u8 [<= 336]
+constexpr int FL_OFF_WSUM = FL_OFF_MASK + 352;                // the live-neuron count
+constexpr int FL_RED_LD = 33;                                 // per-warp down sums: lane l's 32 rows at 33 l + k
+constexpr int FL_RED_W = 32 * FL_RED_LD;                      //   (no bank conflicts on either side)
+constexpr int FL_OFF_RED = FL_OFF_WSUM + 64;                  // per-warp down sums, f32 [12][32][33]
+constexpr int FL_OFF_GATHER = FL_OFF_RED + FL_NW * FL_RED_W * 4;   // rank 0: each CTA's 1024 sums, f32 [S][1024]
+constexpr size_t FL_SMEM = FL_OFF_GATHER + (size_t)FL_MAXS * LAT * 4;
+static_assert(FL_OFF_RED % 16 == 0 && FL_OFF_GATHER % 16 == 0, "fused layer smem alignment");
+
+struct LayerArgs {
+    const uint8_t *slots;
+    int64_t slot_bytes;
+    int64_t nslots;
+    const int32_t *sidx;
+    const int64_t *tab;
+    const float *s2;
+    const float *coef;
+    const void *x;
+    int x_dtype;
+    int K, S;
+    float *h;
+    int32_t *gidx;
+    int32_t *gcnt;
+    float *part;
+    int *status;
+};
+
+__device__ __forceinline__ void st_cluster_f32x4(float *local, uint32_t rank, float4 v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(remote), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_u8(uint8_t *local, uint32_t rank, uint32_t v) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    asm volatile("st.shared::cluster.u8 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
+}
+
+// Block-wide exclusive scan of one int per thread (FL_THREADS threads); returns the exclusive prefix, *total the sum.
+__device__ __forceinline__ int fl_block_scan(int v, int *wsum, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    int excl = inc - v, tot = 0;
+#pragma unroll
+    for (int w = 0; w < FL_NW; ++w) {
+        if (w < warp) excl += wsum[w];
+        tot += wsum[w];
+    }
+    total = tot;
+    __syncthreads();   // wsum may be reused
+    return excl;
+}
+
+template <bool XF32>
+__global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a) {
+    extern __shared__ __align__(16) uint8_t fsm[];
+    float *hs = reinterpret_cast<float *>(fsm + FL_OFF_H);
+    uint16_t *nl = reinterpret_cast<uint16_t *>(fsm + FL_OFF_NL);
+    uint8_t *mk = fsm + FL_OFF_MASK;
+    int *wsum = reinterpret_cast<int *>(fsm + FL_OFF_WSUM);
+    float *red = reinterpret_cast<float *>(fsm + FL_OFF_RED);
+    float *gather = reinterpret_cast<float *>(fsm + FL_OFF_GATHER);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int sr = (int)cluster_ctarank(), j = blockIdx.y, S = a.S;
+    const int npc = INTER / S, ntile = npc / UP_ROWS, ngrp = npc / 16, n0 = sr * npc;
+    cluster_arrive_relaxed();
+
+    pdl_launch_dependents();   // the finish kernel may become resident now; it waits for this grid
+    pdl_wait();                // the layer inputs may be outputs of the preceding kernels
+    const int64_t slot = a.sidx[j];
+    const uint8_t *base = (slot < 0 || slot >= a.nslots) ? nullptr : a.slots + slot * a.slot_bytes;
+    const bool bad = base == nullptr;                 // bad slot: h and every output of the expert NaN
+    const uint8_t *blk = reinterpret_cast<const uint8_t *>(a.tab[j]);
+    const bool bad_tab = blk == nullptr || (reinterpret_cast<uintptr_t>(blk) & 15u) != 0;
+
+    UpArgs xa{};
+    xa.x = a.x;
+    xa.x_dtype = a.x_dtype;
+    UpX<XF32> x;
+    float inv;
+    up_prep_x<XF32>(xa, lane, x, inv);
+    const float mult = a.s2[2 * j] * inv;
+
+    // ---- U: the CTA's up tiles (8 rows each), warp w takes tiles w, w+12, ..., the next tile's loads in flight
+    {
+        int t = warp;
+        UpTile tn;
+        if (t < ntile && !bad) up_load(base, n0 / UP_ROWS + t, lane, tn);
+        for (; t < ntile; t += FL_NW) {
+            const UpTile tc = tn;
+            if (t + FL_NW < ntile && !bad) up_load(base, n0 / UP_ROWS + t + FL_NW, lane, tn);
+            const float u = fmaxf(up_tile_dot<XF32>(tc, x, lane) * mult, 0.f);   // ReLU^2 (qmoe_ns.py:42-44)
+            float hv = u * u;
+            if (bad) hv = __int_as_float(0x7fc00000);
+            const int nloc = t * UP_ROWS + (lane >> 2);
+            const bool lead = (lane & 3) == 0;
+            if (lead) {
+                hs[nloc] = hv;
+                a.h[(int64_t)j * INTER + n0 + nloc] = hv;
+            }
+            const unsigned m = __reduce_or_sync(0xffffffffu, (lead && (hv > 0.f || bad)) ? (1u << (lane >> 2)) : 0u);
+            if (lane == 0) mk[t] = (uint8_t)m;
+            // start bringing the live neurons' dnT_w rows and their groups' dnT_s rows into L2
+            if (!bad_tab && !bad && m) {
+                if (lead && hv > 0.f) {
+                    const uint8_t *row = blk + O_DW + (int64_t)(n0 + nloc) * (LAT / 2);
+#pragma unroll
+                    for (int l = 0; l < 4; ++l) prefetch_l2(row + 128 * l);
+                }
+                if (lane >= 24) prefetch_l2(blk + O_DS + (int64_t)((n0 + t * UP_ROWS) >> 4) * LAT + 128 * (lane - 24));
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- C: each group's live flag (0 / 1) into gidx, which decode_finish_kernel turns into the reference's
+    // ordered list; warp 0 lists the CTA's live neurons, ascending (lane l: groups G*l .. G*l + G - 1)
+    if (tid < ngrp) a.gidx[(int64_t)j * G_DN + sr * ngrp + tid] = (mk[2 * tid] | mk[2 * tid + 1]) != 0;
+    if (warp == 0) {
+        const int G = (ngrp + 31) / 32;
+        int cnt = 0;
+        for (int q = 0; q < G; ++q) {
+            const int g = G * lane + q;
+            if (g < ngrp) cnt += __popc((uint32_t)mk[2 * g] | ((uint32_t)mk[2 * g + 1] << 8));
+        }
+        int inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+        }
+        int o = inc - cnt;
+        for (int q = 0; q < G; ++q) {
+            const int g = G * lane + q;
+            uint32_t mm = g < ngrp ? ((uint32_t)mk[2 * g] | ((uint32_t)mk[2 * g + 1] << 8)) : 0u;
+            while (mm) {
+                const int i = __ffs(mm) - 1;
+                mm &= mm - 1;
+                nl[o++] = (uint16_t)(16 * g + i);
+            }
+        }
+        if (lane == 31) wsum[0] = inc;
+    }
+    __syncthreads();
+    const int L = wsum[0];
+
+    // ---- D: the live neurons' down contributions to all 1024 rows; lane l: rows 32l .. 32l+31
+    float acc[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+    if (!bad_tab) {
+        const uint8_t *wb = blk + O_DW + lane * 16;
+        const uint8_t *sb = blk + O_DS + lane * 32;
+        for (int i0 = warp; i0 < L; i0 += FL_NW * FL_NB) {
+            uint4 wv[FL_NB], s0[FL_NB], s1[FL_NB];
+            float hn[FL_NB];
+#pragma unroll
+            for (int b = 0; b < FL_NB; ++b) {
+                const int i = i0 + b * FL_NW;
+                if (i < L) {
+                    const int nloc = nl[i], n = n0 + nloc;
+                    wv[b] = ldg_stream(wb + (int64_t)n * (LAT / 2));
+                    s0[b] = __ldg(reinterpret_cast<const uint4 *>(sb + (int64_t)(n >> 4) * LAT));
+                    s1[b] = __ldg(reinterpret_cast<const uint4 *>(sb + (int64_t)(n >> 4) * LAT + 16));
+                    hn[b] = hs[nloc];
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < FL_NB; ++b) {
+                if (i0 + b * FL_NW >= L) break;
+                const uint32_t *ww = reinterpret_cast<const uint32_t *>(&wv[b]);
+                const uint32_t sw8[8] = {s0[b].x, s0[b].y, s0[b].z, s0[b].w, s1[b].x, s1[b].y, s1[b].z, s1[b].w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint32_t o[4];
+                    e2m1x8_f16x2(ww[k], o);   // rows 32l + 8k .. 32l + 8k + 7
+                    uint32_t sc[4];
+                    e4m3x4_f16x2(sw8[2 * k], sc[0], sc[1]);
+                    e4m3x4_f16x2(sw8[2 * k + 1], sc[2], sc[3]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(__hmul2(as_h2(o[e]), as_h2(sc[e])));   // exact in f16
+                        acc[8 * k + 2 * e] = fmaf(f.x, hn[b], acc[8 * k + 2 * e]);
+                        acc[8 * k + 2 * e + 1] = fmaf(f.y, hn[b], acc[8 * k + 2 * e + 1]);
+                    }
+                }
+            }
+        }
+    }
+    {
+        float *rw = red + warp * FL_RED_W + lane * FL_RED_LD;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) rw[k] = acc[k];
+    }
+    cluster_wait();   // every CTA of the cluster has started: rank 0's shared memory may be written
+    __syncthreads();
+    // the CTA's sums (warps in order) into rank 0's gather[sr]: thread t sums rows 4t .. 4t+3 (lane t/8 of each warp,
+    // rows 4(t%8) .. 4(t%8)+3 of its 32) and stores them with one 16-byte remote store
+    if (tid < LAT / 4) {
+        const float *rr = red + (tid >> 3) * FL_RED_LD + 4 * (tid & 7);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < FL_NW; ++w) {
+            const float *t = rr + w * FL_RED_W;
+            v.x += t[0], v.y += t[1], v.z += t[2], v.w += t[3];
+        }
+        st_cluster_f32x4(gather + sr * LAT + 4 * tid, 0u, v);
+    }
+    cluster_arrive_release();
+    if (sr != 0) return;   // nothing left for this CTA; rank 0's shared memory is the only one written remotely
+    cluster_wait_acquire();
+
+    // ---- rank 0: part[j], the S CTAs in rank order
+    const float cmul = bad_tab ? __int_as_float(0x7fc00000) : a.coef[j] * a.s2[2 * j + 1];
+    if (tid < LAT / 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < S; ++q) {
+            const float4 t = reinterpret_cast<const float4 *>(gather + q * LAT)[tid];
+            v.x += t.x, v.y += t.y, v.z += t.z, v.w += t.w;
+        }
+        reinterpret_cast<float4 *>(a.part + (int64_t)j * LAT)[tid] = make_float4(v.x * cmul, v.y * cmul, v.z * cmul, v.w * cmul);
+    }
+    if (bad_tab && tid == 0) set_error(a.status, QMOE_ERR_ALIGN);
+}
+
+// A programmatic dependent of decode_layer_kernel: y[r] = sum over experts, in slot order, of part[j][r]; and each
+// expert's live-group list from the 0 / 1 group flags the layer kernel left in gidx (qmoe_ns.py:249-251): live groups
+// ascending, then dead groups ascending, gcnt = the live count (warp w of the grid takes experts w, w + 32, ...).
+__global__ void __launch_bounds__(128) decode_finish_kernel(const float *__restrict__ part, int K, float *__restrict__ y,
+                                                            int32_t *__restrict__ gidx, int32_t *__restrict__ gcnt) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x * 128 + threadIdx.x;
+    float v = 0.f;
+    for (int j0 = 0; j0 < K; j0 += 32) {   // up to 32 independent loads in flight, summed in slot order
+        float t[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) t[k] = j0 + k < K ? __ldcg(part + (int64_t)(j0 + k) * LAT + r) : 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            if (j0 + k < K) v += t[k];
+    }
+    y[r] = v;
+    const int lane = threadIdx.x & 31;
+    for (int j = blockIdx.x * 4 + (threadIdx.x >> 5); j < K; j += 32) {
+        int32_t *gi = gidx + (int64_t)j * G_DN;
+        int f[6], cnt = 0;   // lane l: groups 6l .. 6l + 5
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int g = 6 * lane + q;
+            f[q] = g < G_DN ? __ldcg(gi + g) : 0;
+            cnt += f[q];
+        }
+        int inc = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int t = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += t;
+        }
+        const int total = __shfl_sync(0xffffffffu, inc, 31);
+        int before = inc - cnt;   // live groups before group 6l
+        __syncwarp();             // every lane has read its flags before any list entry is written
+#pragma unroll
+        for (int q = 0; q < 6; ++q) {
+            const int g = 6 * lane + q;
+            if (g < G_DN) gi[f[q] ? before : total + (g - before)] = g;
+            before += f[q];
+        }
+        if (lane == 0) gcnt[j] = total;
     }
 }
 
@@ -775,6 +1092,51 @@ static int launch_down_cluster(const DownArgs &a, cudaStream_t st) {
 static int launch_down_fused(const DownArgs &a, cudaStream_t st, int dev) {
     if (a.K <= DC_MAXK) return launch_down_cluster(a, st);
     return launch_down<true>(a, st, dev, true);
+}
+
+// CTAs per expert of the fused layer: the largest of 8, 7, 6, 4, 3, 2, 1 (2688 / S a multiple of 16) with S * K
+// CTAs fitting the SMs at once; 0 when K exceeds the SMs (the two-kernel form then runs).
+static int layer_split(int K, int sms) {
+    const int opts[7] = {8, 7, 6, 4, 3, 2, 1};
+    for (int i = 0; i < 7; ++i)
+        if (opts[i] * K <= sms) return opts[i];
+    return 0;
+}
+
+static std::atomic<uint64_t> g_fl_smem_b{0}, g_fl_smem_f{0};
+
+// The fused decode-step layer: decode_layer_kernel (clusters of S CTAs per expert) and decode_finish_kernel, both
+// programmatic dependents of what precedes them on the stream.
+static int launch_layer(const LayerArgs &a, float *y, cudaStream_t st, int dev) {
+    const bool f32 = a.x_dtype == QMOE_DT_F32;
+    auto kern = f32 ? decode_layer_kernel<true> : decode_layer_kernel<false>;
+    if (!ensure_smem(kern, FL_SMEM, dev, f32 ? g_fl_smem_f : g_fl_smem_b)) return QMOE_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.S, a.K, 1);
+    cfg.blockDim = dim3(FL_THREADS);
+    cfg.dynamicSmemBytes = FL_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.S;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return QMOE_ERR_LAUNCH;
+    if (int e = launch_status()) return e;
+    cudaLaunchConfig_t cf = {};
+    cf.gridDim = dim3(LAT / 128);
+    cf.blockDim = dim3(128);
+    cf.stream = st;
+    cf.attrs = attr;
+    cf.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cf, decode_finish_kernel, static_cast<const float *>(a.part), a.K, y, a.gidx, a.gcnt) !=
+        cudaSuccess)
+        return QMOE_ERR_LAUNCH;
+    return launch_status();
 }
 
 // Workspace of qmoe_decode_groups: [status int][pad to 64][counters DN_NCHUNK ints][pad][gmask8 K*336 u8]
@@ -864,6 +1226,10 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
     int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);
     uint8_t *gmask8 = ws + WS_GMASK;
     cudaStream_t st = as_stream(stream);
+    if (const int S = layer_split(K, di->sms)) {   // one fused kernel per layer (+ the expert sum)
+        LayerArgs la{slots_up, slot_bytes, nslots, sidx, tab, s2, coef, x, x_dtype, K, S, h, gidx, gcnt, part, status};
+        return launch_layer(la, y, st, dev);
+    }
     UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
@@ -970,6 +1336,10 @@ int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64
     int *counters = reinterpret_cast<int *>(ws + WS_COUNTERS);   // zeroed by the up kernel on every call
     uint8_t *gmask8 = ws + WS_GMASK;                              // rewritten in full on every call
     cudaStream_t st = as_stream(stream);
+    if (const int S = layer_split(K, di->sms)) {   // one fused kernel per layer (+ the expert sum)
+        LayerArgs la{slots_up, slot_bytes, nslots, sidx, tab, s2, coef, x, x_dtype, K, S, h, gidx, gcnt, part, status};
+        return launch_layer(la, y, st, dev);
+    }
     UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};

@@ -421,11 +421,12 @@ def test_decode_groups_large_K_two_kernel_path(Q, experts, oracle_decode):
     assert np.array_equal(gidx.cpu().numpy(), og) and np.array_equal(gcnt.cpu().numpy(), oc)
 
 
-@pytest.mark.parametrize("K", [1, 4, 8, 9, 31, 32, 33])
+@pytest.mark.parametrize("K", [1, 4, 8, 9, 19, 25, 31, 33, 38, 49, 75, 148, 150])
 def test_decode_groups_K_range(Q, experts, K):
-    """moe_decode_groups for K experts (entry j -> expert j mod 22): K <= 32 takes the cluster form of the down
-    kernel (CTAs of 1-4 experts, empty CTAs when K < 8), K = 33 the arrival-counter form; y within 1e-5 of the
-    fp64 oracle, gidx / gcnt the exact compaction of the kernel's h."""
+    """moe_decode_groups for K experts (entry j -> expert j mod 22). Up to the SM count (148) the fused layer kernel
+    runs with S = 8, 7, 6, 4, 3, 2 or 1 CTAs per expert (each S is taken by one of these K); K = 150 takes the
+    up kernel + arrival-counter down kernel. y and the per-expert outputs within 1e-5 of the fp64 oracle, gidx /
+    gcnt the exact compaction of the kernel's h."""
     e = experts
     T, tab, _ = _T_setup(Q, e)
     idx = torch.arange(K, device=DEV) % 22

@@ -4,12 +4,13 @@ allocation calls, foreign-language hosts that only pass pointers through). It ke
 static device array inside the library instead of a caller workspace.
 
 Checked here through the C ABI against the workspace entry point qmoe_decode_groups on the same inputs. Both
-run the same two kernels with the same fixed summation order, so every output must be bit-identical:
-  - two calls in a row (the second finds the first call's leftovers in the shared array), K = 22;
-  - K = 80: experts past the 64 whose metadata the up kernel stages in shared memory take its
-    global-memory path; also within 1e-5 of the fp64 oracle;
-  - the workspace entry point on a workspace whose arrival counters hold garbage: the up kernel must clear
-    them, or the down kernel's last-arriving CTA never sums y;
+run the same kernels with the same fixed summation order, so every output must be bit-identical:
+  - two calls in a row (the second finds the first call's leftovers in the shared array), K = 22 (the fused
+    layer kernel, 6 CTAs per expert);
+  - K = 80 (one CTA per expert); also within 1e-5 of the fp64 oracle;
+  - the workspace entry point at K = 150 (more experts than SMs: the up kernel + arrival-counter down kernel)
+    on a workspace whose arrival counters hold garbage: the up kernel must clear them, or the down kernel's
+    last-arriving CTA never sums y;
   - a misaligned tab entry: that expert's part row and y are NaN, the static status word reads
     QMOE_ERR_ALIGN through qmoe_decode_groups_static_status and clears, and the next call is clean;
   - K above the static limit is refused before any work.
@@ -112,16 +113,19 @@ def test_static_entry_point_matches_workspace_entry_point(layer, K):
 
 
 def test_workspace_counters_left_dirty_are_cleared(layer):
-    """The arrival counters of a workspace (bytes 64..95) filled with garbage, the status word zero: the up kernel
-    clears them before the down kernel counts, so the result equals that of a clean workspace."""
+    """K = 150 (more experts than SMs: the up kernel + arrival-counter down kernel, whose counters live in the
+    workspace): the counters (bytes 64..95) filled with garbage, the status word zero. The up kernel clears them
+    before the down kernel counts, so the result equals that of a clean workspace."""
     import _qmoe_lib as C
     L = layer
-    c = _case(L, 22)
+    K = 150
+    L = dict(layer, coef=(torch.arange(K, device=DEV, dtype=torch.float32) % 7 + 1) / 7)
+    c = _case(L, K)
     x = L["xs"][0]
-    clean, dirty = _bufs(22), _bufs(22)
-    ws = _workspace(22)
+    clean, dirty = _bufs(K), _bufs(K)
+    ws = _workspace(K)
     assert _call("qmoe_decode_groups", L, c, x, clean, (C.ptr(ws), ws.numel())) == 0
-    ws2 = _workspace(22)
+    ws2 = _workspace(K)
     ws2[64:96] = 0x5A
     assert _call("qmoe_decode_groups", L, c, x, dirty, (C.ptr(ws2), ws2.numel())) == 0
     torch.cuda.synchronize()
