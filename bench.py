@@ -13,8 +13,8 @@ step is served from L2.
   e2e   : the same step through the public API with host buffers, layer by layer as the model runs it: per
           layer, the H2D copy of that layer's routed inputs from pinned host memory, the layer call, and the
           D2H copy of its output (layer m+1's input depends on layer m's output in the real model).
-  roofline: the up GEMV kernel (the dominant kernel), timed live with CUDA events over the timed region,
-          against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+  roofline: the fused layer kernel (decode_layer_kernel + its finish kernel), per layer, from the CUDA events
+          of the timed region, against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
   prefill (N = 1): BASELINE config 3, one 512-expert layer, T = 2048 (and T = 64) tokens through
           qmoe_prefill_grouped: tokens/s, roofline, e2e, CPU baseline, clocks.
   ep (every N): BASELINE config 4, expert parallelism over the N ranks (512 / N experts of every layer per
@@ -41,9 +41,10 @@ sys.path.insert(0, os.path.join(ROOT, "nemotron-super-8gb_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE decode us/token (40-layer routed-expert decode, bs=1)"
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one decode_up_kernel launch at K = 22, from a
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one decode_layer_kernel launch at K = 22, from a
 # single-launch ncu capture of this workload; ncu cannot run inside the timed bench, so the figure is carried here
-UP_TRAFFIC_NCU = 34082560 + 768
+# (None until a capture of the current kernel is summarised)
+LAYER_TRAFFIC_NCU = None
 N_LAYERS, NE, K = 40, 512, 22
 N_TOK = 64
 
@@ -991,36 +992,15 @@ def main():
     us_per_token = ms * 1e3 / (args.steps * world)
     us_per_token_rank = ms * 1e3 / args.steps
 
-    # ---- the dominant kernel (up GEMV) timed live with events on its stream: a graph of the 40 up
-    # launches of one token (inputs resident), replayed between two events; per-launch time =
-    # elapsed / launches (graph launch gaps included, so this slightly overstates a launch).
-    up_fn = C.lib().qmoe_decode_up
-    up_graphs = []
-    for t in range(4):
-        gu = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gu, stream=stream):
-            for m in range(L):
-                rc = up_fn(store.data_ptr(), store.stride(0), store.shape[0], T["SIDX"][t, m].data_ptr(), K,
-                           T["S2"][t, m].data_ptr(), T["X"][t, m].data_ptr(), 1, step.h[m].data_ptr(),
-                           stream.cuda_stream)
-                assert rc == 0
-        up_graphs.append(gu)
-    with torch.cuda.stream(stream):
-        for gu in up_graphs:
-            gu.replay()
-        u0 = torch.cuda.Event(enable_timing=True)
-        u1 = torch.cuda.Event(enable_timing=True)
-        reps = 20
-        u0.record(stream)
-        for r in range(reps):
-            up_graphs[r % 4].replay()
-        u1.record(stream)
-        u1.synchronize()
-    up_ms = [u0.elapsed_time(u1) / (reps * L)]
-    up_bytes = K * 1548288 + 2048 + K * S.INTER * 4
-    up_us = statistics.mean(up_ms) * 1e3
+    # ---- the dominant kernel: decode_layer_kernel (up GEMV + ReLU^2 + live-neuron down GEMV of every expert,
+    # one cluster per expert), with decode_finish_kernel (the 1024-row sum over experts) after it as its
+    # programmatic dependent. The pair is timed as the layer it forms, from the CUDA events of the timed region
+    # (device time per layer = step time / layers), against the layer's algorithmic bytes: every routed expert's
+    # up half, the live neurons' dnT_w rows and live groups' dnT_s rows, x and y.
+    layer_us = us_per_token_rank / L
+    layer_bytes = bytes_per_token / L
     hbm, peak_kind = peaks()
-    up_gbs = up_bytes / (up_us * 1e-6) / 1e9
+    layer_gbs = layer_bytes / (layer_us * 1e-6) / 1e9
 
     # ---- e2e through the public path with host buffers, layer by layer as the model runs it: per layer one H2D
     # copy of that layer's packed routed inputs (x, slot ids, block addresses, s2, weights) from pinned host memory,
@@ -1106,11 +1086,12 @@ def main():
             "live_fraction": round(live_frac, 4),
             "hbm_gbs_step": round(step_gbs, 1), "hbm_frac_step": round(step_gbs / hbm, 4),
             "bytes_per_token": int(bytes_per_token),
-            "roofline": {"kernel": "decode_up_kernel", "bound": "hbm", "achieved": round(up_gbs, 1), "peak": hbm,
-                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(up_gbs / hbm, 4),
-                         "traffic": UP_TRAFFIC_NCU,
-                         "traffic_source": "ncu single-launch capture of this kernel at K=22 (DRAM read + write)",
-                         "bytes_per_launch": up_bytes, "us_per_launch": round(up_us, 3)},
+            "roofline": {"kernel": "decode_layer_kernel + decode_finish_kernel (one layer)", "bound": "hbm",
+                         "achieved": round(layer_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(layer_gbs / hbm, 4), "traffic": LAYER_TRAFFIC_NCU,
+                         "traffic_source": "ncu single-launch capture of decode_layer_kernel (DRAM read + write), "
+                                           "a 22-expert layer at the mean live fraction",
+                         "bytes_per_launch": int(layer_bytes), "us_per_launch": round(layer_us, 3)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/token", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "copies": "per layer: one H2D of its inputs, one D2H of y",
                     "matches_device_path": e2e_ok},
@@ -1119,7 +1100,7 @@ def main():
             "cpu_baseline": cpu,
             "build_s": round(t_build, 1),
         }
-    del graphs, g_e2e, up_graphs, step, store, T
+    del graphs, g_e2e, step, store, T
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
 

@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(DC_TPE * DC_MAXE) decode_down_cluster_kernel(D
 // * h. So no CTA waits for another's up tiles, and the down work of early CTAs overlaps the up tail of late ones.
 // The CTA's 1024 partial sums (its 12 warps in order) and its groups' live flags go to cluster rank 0's shared
 // memory; rank 0 sums the S CTAs in rank order into part[j] (x coef_j * s2d_j) and writes gidx / gcnt for the
-// expert. decode_finish_kernel, a programmatic dependent, sums the experts in slot order into y.
+// expert. decode_finish_kernel, its programmatic dependent, sums the experts in slot order into y.
 constexpr int FL_NW = UP_NW;                   // 12 warps, as the up kernel
 constexpr int FL_THREADS = 32 * FL_NW;
 constexpr int FL_MAXS = 8;                     // CTAs per expert (portable cluster size)
@@ -734,7 +734,8 @@ constexpr int FL_NB = 4;                       // live neurons per warp with all
 constexpr int FL_OFF_H = 0;                                   // h of the CTA's neurons, f32 [<= 2688]
 constexpr int FL_OFF_NL = FL_OFF_H + INTER * 4;               // live neurons (CTA-local index), u16 [<= 2688]
 constexpr int FL_OFF_MASK = FL_OFF_NL + INTER * 2;            // live mask per 8-row tile, u8 [<= 336]
-constexpr int FL_OFF_WSUM = FL_OFF_MASK + 352;                // the live-neuron count
+constexpr int FL_OFF_TMASK = FL_OFF_MASK + 352;               // rank 0: the expert's 336 tile masks (all CTAs)
+constexpr int FL_OFF_WSUM = FL_OFF_TMASK + 352;               // the live-neuron count
 constexpr int FL_RED_LD = 33;                                 // per-warp down sums: lane l's 32 rows at 33 l + k
 constexpr int FL_RED_W = 32 * FL_RED_LD;                      //   (no bank conflicts on either side)
 constexpr int FL_OFF_RED = FL_OFF_WSUM + 64;                  // per-warp down sums, f32 [12][32][33]
@@ -801,6 +802,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
     float *hs = reinterpret_cast<float *>(fsm + FL_OFF_H);
     uint16_t *nl = reinterpret_cast<uint16_t *>(fsm + FL_OFF_NL);
     uint8_t *mk = fsm + FL_OFF_MASK;
+    uint8_t *tmask = fsm + FL_OFF_TMASK;
     int *wsum = reinterpret_cast<int *>(fsm + FL_OFF_WSUM);
     float *red = reinterpret_cast<float *>(fsm + FL_OFF_RED);
     float *gather = reinterpret_cast<float *>(fsm + FL_OFF_GATHER);
@@ -858,9 +860,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
     }
     __syncthreads();
 
-    // ---- C: each group's live flag (0 / 1) into gidx, which decode_finish_kernel turns into the reference's
-    // ordered list; warp 0 lists the CTA's live neurons, ascending (lane l: groups G*l .. G*l + G - 1)
-    if (tid < ngrp) a.gidx[(int64_t)j * G_DN + sr * ngrp + tid] = (mk[2 * tid] | mk[2 * tid + 1]) != 0;
+    // ---- C: warp 0 lists the CTA's live neurons, ascending (lane l: groups G*l .. G*l + G - 1)
     if (warp == 0) {
         const int G = (ngrp + 31) / 32;
         int cnt = 0;
@@ -951,6 +951,7 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
         }
         st_cluster_f32x4(gather + sr * LAT + 4 * tid, 0u, v);
     }
+    if (tid < ntile) st_cluster_u8(tmask + sr * ntile + tid, 0u, mk[tid]);   // the CTA's tile masks, for gidx
     cluster_arrive_release();
     if (sr != 0) return;   // nothing left for this CTA; rank 0's shared memory is the only one written remotely
     cluster_wait_acquire();
@@ -965,35 +966,14 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
         }
         reinterpret_cast<float4 *>(a.part + (int64_t)j * LAT)[tid] = make_float4(v.x * cmul, v.y * cmul, v.z * cmul, v.w * cmul);
     }
-    if (bad_tab && tid == 0) set_error(a.status, QMOE_ERR_ALIGN);
-}
-
-// A programmatic dependent of decode_layer_kernel: y[r] = sum over experts, in slot order, of part[j][r]; and each
-// expert's live-group list from the 0 / 1 group flags the layer kernel left in gidx (qmoe_ns.py:249-251): live groups
-// ascending, then dead groups ascending, gcnt = the live count (warp w of the grid takes experts w, w + 32, ...).
-__global__ void __launch_bounds__(128) decode_finish_kernel(const float *__restrict__ part, int K, float *__restrict__ y,
-                                                            int32_t *__restrict__ gidx, int32_t *__restrict__ gcnt) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int r = blockIdx.x * 128 + threadIdx.x;
-    float v = 0.f;
-    for (int j0 = 0; j0 < K; j0 += 32) {   // up to 32 independent loads in flight, summed in slot order
-        float t[32];
-#pragma unroll
-        for (int k = 0; k < 32; ++k) t[k] = j0 + k < K ? __ldcg(part + (int64_t)(j0 + k) * LAT + r) : 0.f;
-#pragma unroll
-        for (int k = 0; k < 32; ++k)
-            if (j0 + k < K) v += t[k];
-    }
-    y[r] = v;
-    const int lane = threadIdx.x & 31;
-    for (int j = blockIdx.x * 4 + (threadIdx.x >> 5); j < K; j += 32) {
-        int32_t *gi = gidx + (int64_t)j * G_DN;
-        int f[6], cnt = 0;   // lane l: groups 6l .. 6l + 5
+    if (warp == FL_NW - 1) {
+        // the expert's live-group list (qmoe_ns.py:249-251): live groups ascending, then dead groups ascending;
+        // lane l takes groups 6l .. 6l+5, a group live if either of its two tiles has a live neuron
+        int f[6], cnt = 0;
 #pragma unroll
         for (int q = 0; q < 6; ++q) {
             const int g = 6 * lane + q;
-            f[q] = g < G_DN ? __ldcg(gi + g) : 0;
+            f[q] = g < G_DN ? ((tmask[2 * g] | tmask[2 * g + 1]) != 0) : 0;
             cnt += f[q];
         }
         int inc = cnt;
@@ -1004,15 +984,34 @@ __global__ void __launch_bounds__(128) decode_finish_kernel(const float *__restr
         }
         const int total = __shfl_sync(0xffffffffu, inc, 31);
         int before = inc - cnt;   // live groups before group 6l
-        __syncwarp();             // every lane has read its flags before any list entry is written
 #pragma unroll
         for (int q = 0; q < 6; ++q) {
             const int g = 6 * lane + q;
-            if (g < G_DN) gi[f[q] ? before : total + (g - before)] = g;
+            if (g < G_DN) a.gidx[(int64_t)j * G_DN + (f[q] ? before : total + (g - before))] = g;
             before += f[q];
         }
-        if (lane == 0) gcnt[j] = total;
+        if (lane == 0) a.gcnt[j] = total;
     }
+    if (bad_tab && tid == 0) set_error(a.status, QMOE_ERR_ALIGN);
+
+}
+
+// y[r] = sum over experts, in slot order, of part[j][r]: a programmatic dependent of decode_layer_kernel, all K loads
+// of a row in flight at once (32 at a time).
+__global__ void __launch_bounds__(128) decode_finish_kernel(const float *__restrict__ part, int K, float *__restrict__ y) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int r = blockIdx.x * 128 + threadIdx.x;
+    float v = 0.f;
+    for (int j0 = 0; j0 < K; j0 += 32) {
+        float t[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) t[k] = j0 + k < K ? __ldcg(part + (int64_t)(j0 + k) * LAT + r) : 0.f;
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+            if (j0 + k < K) v += t[k];
+    }
+    y[r] = v;
 }
 
 // ------------------------------------------------------------------ sum over experts (orig-layout path)
@@ -1133,8 +1132,7 @@ static int launch_layer(const LayerArgs &a, float *y, cudaStream_t st, int dev) 
     cf.stream = st;
     cf.attrs = attr;
     cf.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cf, decode_finish_kernel, static_cast<const float *>(a.part), a.K, y, a.gidx, a.gcnt) !=
-        cudaSuccess)
+    if (cudaLaunchKernelEx(&cf, decode_finish_kernel, static_cast<const float *>(a.part), a.K, y) != cudaSuccess)
         return QMOE_ERR_LAUNCH;
     return launch_status();
 }
