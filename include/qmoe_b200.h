@@ -86,9 +86,12 @@ int qmoe_decode_down_groups(const int64_t *tab, const float *h, const int32_t *g
  *   y[r] = sum_j coef[j] * s2[j,1] * (D_j h_j)[r].
  * Outputs: h [K,2688] f32, gidx [K,168] i32, gcnt [K] i32 (as the reference leaves them), y [1024] f32;
  * part [K,1024] f32 receives the per-expert outputs coef_j*s2d_j*D_j h_j (the reference's part_buf[0,:K]).
- * Two kernels: the up GEMV, then the live-group down GEMV launched as its programmatic dependent; the
- * last CTA of each 128-row chunk sums the K experts in slot order. The workspace (size from
- * qmoe_decode_groups_workspace_bytes) must not be used by another call running concurrently. */
+ * Every sum is fp32; results are bit-identical from call to call. For K up to the SM count one kernel per
+ * layer (each expert's neurons over a cluster of CTAs that stream their up rows and add their own live
+ * neurons' down rows) and a small kernel summing the experts in slot order; above it, the up GEMV and the
+ * live-group down GEMV. Both launch as programmatic dependents of the preceding work on `stream`. The
+ * workspace (size from qmoe_decode_groups_workspace_bytes, zero-filled once) must not be used by another
+ * call running concurrently. */
 size_t qmoe_decode_groups_workspace_bytes(int K);
 int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
                        const int64_t *tab,

@@ -1,18 +1,20 @@
-// Decode-step routed-expert kernels (bs = 1) for sm_100a.
+// Decode-step routed-expert kernels (bs = 1) for sm_100a. Every sum is fp32, as in the reference's kernels.
 //
-//   decode_up_kernel    — `_up` (qmoe_ns.py:24-44): one CTA per SM, 16 warps; a warp takes whole 8-row tiles
-//                         and streams each row's 512 B of codes with 16-byte loads (a lane's 16 B of every
-//                         row of the tile in flight at once), keeps its 32-element slice of x in registers as
-//                         prescaled f16x2, decodes with cvt.e2m1x2, reduces the 8 rows with a 9-shuffle
-//                         butterfly. Fused epilogue: ReLU^2, h, and the tile's 8-bit live-neuron mask, so no
-//                         separate liveness pass is needed; live neurons' down rows are prefetched to L2.
+//   decode_layer_kernel — `moe_decode_groups` (qmoe_ns.py:245-255) for K <= SMs, one kernel per layer: each expert's
+//                         neurons split over a cluster of S CTAs; a CTA streams its up rows (`_up`, qmoe_ns.py:24-44),
+//                         keeps h and the live masks on chip and adds its own live neurons' down rows (`_down_groups`,
+//                         qmoe_ns.py:209-239, T layout); the cluster's sums meet in rank 0 over distributed shared
+//                         memory, which writes part[j] and the expert's live-group lists (qmoe_ns.py:249-251).
+//   decode_finish_kernel — its programmatic dependent: y = the experts' outputs summed in slot order.
+//   decode_up_kernel    — `_up` alone (qmoe_decode_up, qmoe_decode, and the layer for K above the SM count): one CTA
+//                         per SM, 12 warps; a warp takes whole 8-row tiles, a lane 16 B of each row and a 32-element
+//                         slice of x, the next tile's loads in flight during the current tile's math; ReLU^2, h and
+//                         the tile's 8-bit live-neuron mask; live neurons' down rows prefetched to L2.
 //   live_groups_kernel  — the torch glue of moe_decode_groups (qmoe_ns.py:249-251).
-//   decode_down_kernel  — `_down_groups` (qmoe_ns.py:209-239) over the T layout: CTA = (expert, split,
-//                         128-row chunk); compacts the live groups and live neurons into shared memory,
-//                         streams 64 B of codes per live neuron and 128 B of scales per live group, and
-//                         reduces the 64 neuron slots in a fixed order. In the fused form the last CTA of
-//                         each chunk (arrival counter) sums the K experts in slot order into y, so the
-//                         result is deterministic without float atomics.
+//   decode_down_kernel  — `_down_groups` over the T layout for the reference form (qmoe_decode_down_groups, KS splits)
+//                         and for the layer above the SM count: CTA = (128-row chunk, split, expert); live neurons
+//                         compacted into shared memory; in the fused form the last CTA of each chunk (arrival counter)
+//                         sums the K experts in slot order into y.
 #include "common.cuh"
 #include "gemv.cuh"
 #include "host.h"
@@ -486,42 +488,16 @@ __global__ void __launch_bounds__(DN_THREADS) decode_down_kernel(DownArgs a) {
     }
 }
 
-// ------------------------------------------------------------------ down over live groups, cluster form (K <= 32)
-// `_down_groups` (qmoe_ns.py:209-239) + the fixed-order sum over experts for the decode-step layer, without a
-// GPU-scope fence or arrival atomic on the critical path. A cluster of DC_CL CTAs owns one 32-row output chunk;
-// CTA c of the cluster takes experts c, c + DC_CL, ... with 64 threads per expert (K = 22: 6 experts, 384
-// threads, one CTA per SM on 128 SMs). Per expert: the 168 16-bit group masks from the up kernel, a 64-thread scan
-// listing the live neurons (ascending), then thread u takes neurons u, u+64, ... (16 B of codes = the chunk's 32
-// rows, the group's 32 scale bytes, h; up to DC_NB neurons' loads in flight at once), fp32 accumulation of
-// (e2m1 * e4m3, exact in f16) * h, a 31-shuffle transpose-reduce per warp and a fixed-order sum of the 2 warps.
-// The CTA adds its experts in order; cluster rank 0 adds the DC_CL CTAs' sums in rank order: each CTA pushes its
-// sum into rank 0's shared memory and arrives on the cluster barrier; only rank 0 waits.
-// (Measured on B200, 40-layer decode: clusters of 4 with the push model 657 us/token; with two barriers and
-// rank 0 pulling 667; clusters of 8 813-881 (as programmatic dependents their launch is late); 16-row chunks or
-// 96-128 threads per expert 696-845; the arrival-counter form 703.)
-constexpr int DC_ROWS = 32;                 // output rows per CTA (16 or 32): ROWS/2 code bytes per neuron
-constexpr int DC_NCH = LAT / DC_ROWS;       // 32 chunks
-constexpr int DC_CL = 4;                    // CTAs per cluster
-constexpr int DC_TPE = 64;                  // threads per expert (a multiple of 32, at least 42)
-constexpr int DC_MAXE = 8;                  // experts per CTA: K <= DC_CL * DC_MAXE
-constexpr int DC_MAXK = DC_CL * DC_MAXE;    // 32
-constexpr int DC_NB = 4;                    // neurons per thread with all loads in flight at once
-
+// ------------------------------------------------------------------ thread-block-cluster helpers
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
 
-// Store v into the shared variable `local` of CTA `rank` of the cluster (st.shared::cluster at the mapa address).
-__device__ __forceinline__ void st_cluster_f32(float *local, uint32_t rank, float v) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
-}
-
-// Split cluster barrier at kernel entry: every CTA arrives at once and waits just before its first access to another
-// CTA's shared memory, which must not happen before all CTAs of the cluster have started.
+// Cluster barrier (split): every CTA arrives at kernel entry and waits just before its first access to another CTA's
+// shared memory, which must not happen before all CTAs of the cluster have started; the release / acquire pair at the
+// end publishes the pushed sums to rank 0.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
@@ -536,183 +512,6 @@ __device__ __forceinline__ void cluster_arrive_release() {
 
 __device__ __forceinline__ void cluster_wait_acquire() {
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void named_bar(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__global__ void __launch_bounds__(DC_TPE * DC_MAXE) decode_down_cluster_kernel(DownArgs a) {
-    __shared__ uint16_t nl[DC_MAXE][INTER];          // live neurons of each of the CTA's experts
-    __shared__ int s_wsum[DC_MAXE][DC_TPE / 32];
-    __shared__ float red[DC_MAXE][DC_TPE / 32][DC_ROWS];
-    __shared__ float pe[DC_MAXE][DC_ROWS];           // per-expert outputs of the chunk
-    __shared__ float gather[DC_CL][DC_ROWS];         // rank 0: each CTA's sum of its experts, by rank
-
-    const int tid = threadIdx.x, el = tid / DC_TPE, u = tid % DC_TPE, w = u >> 5, lane = tid & 31;
-    const int c = (int)cluster_ctarank(), rc = blockIdx.y;
-    const int nexp = blockDim.x / DC_TPE;
-    const int j = c + DC_CL * el;                    // this thread's expert
-    const bool has = j < a.K;
-
-    const uint8_t *blk = has ? reinterpret_cast<const uint8_t *>(a.tab[j]) : nullptr;
-    const bool bad = has && ((reinterpret_cast<uintptr_t>(blk) & 15u) != 0 || blk == nullptr);
-    const float cmul = has ? a.coef[j] * a.s2[2 * j + 1] : 0.f;
-    cluster_arrive_relaxed();
-
-    pdl_launch_dependents();   // the next kernel (the next layer's up) may start its launch now
-    pdl_wait();                // the up kernel's h and masks are complete and visible
-
-    // ---- 1. live neurons of expert j, ascending: thread u < 42 takes groups 4u .. 4u+3; one 64-thread scan of
-    // packed (live-group count << 16 | live-neuron count) gives each its offset in nl and the groups' ranks.
-    uint2 m4 = make_uint2(0u, 0u);   // four 16-bit group masks
-    if (has && u < G_DN / 4) m4 = *reinterpret_cast<const uint2 *>(a.gmask8 + (int64_t)j * 2 * G_DN + 8 * u);
-    const uint32_t gm[4] = {m4.x & 0xFFFFu, m4.x >> 16, m4.y & 0xFFFFu, m4.y >> 16};
-    const int packed = (((gm[0] != 0) + (gm[1] != 0) + (gm[2] != 0) + (gm[3] != 0)) << 16) | (__popc(m4.x) + __popc(m4.y));
-    int inc = packed;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += v;
-    }
-    if (lane == 31) s_wsum[el][w] = inc;
-    named_bar(1 + el, DC_TPE);
-    int excl = inc - packed, tot = 0;
-#pragma unroll
-    for (int ww = 0; ww < DC_TPE / 32; ++ww) {
-        if (ww < w) excl += s_wsum[el][ww];
-        tot += s_wsum[el][ww];
-    }
-    {
-        int off = excl & 0xFFFF;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t mm = gm[q];
-            while (mm) {
-                const int i = __ffs(mm) - 1;
-                mm &= mm - 1;
-                nl[el][off++] = (uint16_t)(64 * u + 16 * q + i);
-            }
-        }
-    }
-    if (has && rc == 0 && u < G_DN / 4) {   // gidx / gcnt as the reference's glue leaves them (qmoe_ns.py:249-251)
-        const int total_groups = tot >> 16;
-        int gr = excl >> 16;   // live groups before group 4u
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int g = 4 * u + q;
-            a.gidx_out[(int64_t)j * G_DN + (gm[q] ? gr : total_groups + (g - gr))] = g;
-            gr += gm[q] != 0;
-        }
-        if (u == 0) a.gcnt_out[j] = total_groups;
-    }
-    named_bar(1 + el, DC_TPE);
-    const int L = tot & 0xFFFF;
-
-    // ---- 2. stream the live neurons: DC_ROWS/2 bytes of codes (rows DC_ROWS*rc ..), the group's DC_ROWS scale
-    // bytes, h
-    constexpr int CW = DC_ROWS / 8;   // 32-bit words of codes per neuron (8 rows each)
-    float acc[DC_ROWS];
-#pragma unroll
-    for (int k = 0; k < DC_ROWS; ++k) acc[k] = 0.f;
-    if (has && !bad) {
-        const uint8_t *wb = blk + O_DW + rc * (DC_ROWS / 2);
-        const uint8_t *sb = blk + O_DS + rc * DC_ROWS;
-        const float *hj = a.h + (int64_t)j * INTER;
-        for (int i0 = u; i0 < L; i0 += DC_TPE * DC_NB) {
-            uint32_t wv[DC_NB][CW], sv[DC_NB][2 * CW];
-            float hn[DC_NB];
-#pragma unroll
-            for (int b = 0; b < DC_NB; ++b) {
-                const int i = i0 + b * DC_TPE;
-                if (i < L) {
-                    const int n = nl[el][i];
-                    const uint8_t *wp = wb + (int64_t)n * (LAT / 2);
-                    const uint8_t *sp = sb + (int64_t)(n >> 4) * LAT;
-                    if constexpr (DC_ROWS == 32) {
-                        const uint4 w4 = ldg_stream(wp);
-                        wv[b][0] = w4.x, wv[b][1] = w4.y, wv[b][2] = w4.z, wv[b][3] = w4.w;
-                        const uint4 s0 = __ldg(reinterpret_cast<const uint4 *>(sp));
-                        const uint4 s1 = __ldg(reinterpret_cast<const uint4 *>(sp + 16));
-                        sv[b][0] = s0.x, sv[b][1] = s0.y, sv[b][2] = s0.z, sv[b][3] = s0.w;
-                        sv[b][4] = s1.x, sv[b][5] = s1.y, sv[b][6] = s1.z, sv[b][7] = s1.w;
-                    } else {
-                        const uint2 w2 = __ldg(reinterpret_cast<const uint2 *>(wp));
-                        wv[b][0] = w2.x, wv[b][1] = w2.y;
-                        const uint4 s0 = __ldg(reinterpret_cast<const uint4 *>(sp));
-                        sv[b][0] = s0.x, sv[b][1] = s0.y, sv[b][2] = s0.z, sv[b][3] = s0.w;
-                    }
-                    hn[b] = hj[n];
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < DC_NB; ++b) {
-                if (i0 + b * DC_TPE >= L) break;
-#pragma unroll
-                for (int k = 0; k < CW; ++k) {
-                    uint32_t o[4];
-                    e2m1x8_f16x2(wv[b][k], o);   // rows 8k .. 8k+7 of the chunk
-                    uint32_t sc[4];
-                    e4m3x4_f16x2(sv[b][2 * k], sc[0], sc[1]);
-                    e4m3x4_f16x2(sv[b][2 * k + 1], sc[2], sc[3]);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __half22float2(__hmul2(as_h2(o[e]), as_h2(sc[e])));   // exact in f16
-                        acc[8 * k + 2 * e] = fmaf(f.x, hn[b], acc[8 * k + 2 * e]);
-                        acc[8 * k + 2 * e + 1] = fmaf(f.y, hn[b], acc[8 * k + 2 * e + 1]);
-                    }
-                }
-            }
-        }
-    }
-
-    // ---- 3. fixed-order reduction: transpose-reduce in each warp (lane r ends with row r % DC_ROWS), then the
-    // warps in order
-#pragma unroll
-    for (int sft = DC_ROWS / 2; sft >= 1; sft >>= 1) {
-        const bool upper = lane & sft;
-#pragma unroll
-        for (int i = 0; i < sft; ++i) {
-            const float send = upper ? acc[i] : acc[i + sft];
-            const float keep = upper ? acc[i + sft] : acc[i];
-            acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, sft);
-        }
-    }
-    if constexpr (DC_ROWS == 16) acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 16);
-    if (lane < DC_ROWS) red[el][w][lane] = acc[0];
-    named_bar(1 + el, DC_TPE);
-    if (has && u < DC_ROWS) {
-        float v = 0.f;
-#pragma unroll
-        for (int ww = 0; ww < DC_TPE / 32; ++ww) v += red[el][ww][u];
-        float out = v * cmul;
-        if (bad) out = __int_as_float(0x7fc00000);
-        pe[el][u] = out;
-        a.part[(int64_t)j * LAT + rc * DC_ROWS + u] = out;
-        if (bad && u == 0) set_error(a.status, QMOE_ERR_ALIGN);
-    }
-    __syncthreads();
-    // ---- 4. every CTA stores the sum of its experts (in order) into cluster rank 0's gather[c] (distributed shared
-    // memory) and arrives on the cluster barrier with release semantics; rank 0 waits for all arrivals and sums the
-    // CTAs in rank order. Only rank 0 waits: the others have nothing left to do and exit (a cluster-barrier wait
-    // counts only threads that have not exited), while rank 0, the only CTA whose shared memory is written
-    // remotely, stays until it has read it.
-    cluster_wait();   // every CTA of the cluster has started
-    if (tid < DC_ROWS) {
-        float v = 0.f;
-        for (int e = 0; e < nexp && c + DC_CL * e < a.K; ++e) v += pe[e][tid];
-        st_cluster_f32(&gather[c][tid], 0u, v);
-    }
-    cluster_arrive_release();
-    if (c == 0) {
-        cluster_wait_acquire();
-        if (tid < DC_ROWS) {
-            float v = 0.f;
-#pragma unroll
-            for (int r = 0; r < DC_CL; ++r) v += gather[r][tid];
-            a.y[rc * DC_ROWS + tid] = v;
-        }
-    }
 }
 
 // ------------------------------------------------------------------ the decode-step layer fused per CTA
@@ -772,28 +571,6 @@ __device__ __forceinline__ void st_cluster_u8(uint8_t *local, uint32_t rank, uin
     uint32_t remote;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
     asm volatile("st.shared::cluster.u8 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
-}
-
-// Block-wide exclusive scan of one int per thread (FL_THREADS threads); returns the exclusive prefix, *total the sum.
-__device__ __forceinline__ int fl_block_scan(int v, int *wsum, int &total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int inc = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += t;
-    }
-    if (lane == 31) wsum[warp] = inc;
-    __syncthreads();
-    int excl = inc - v, tot = 0;
-#pragma unroll
-    for (int w = 0; w < FL_NW; ++w) {
-        if (w < warp) excl += wsum[w];
-        tot += wsum[w];
-    }
-    total = tot;
-    __syncthreads();   // wsum may be reused
-    return excl;
 }
 
 template <bool XF32>
@@ -1066,33 +843,6 @@ static int launch_down(const DownArgs &a, cudaStream_t st, int dev, bool pdl) {
     return launch_status();
 }
 
-// The cluster form of the fused down kernel (K <= DC_MAXK), launched as a programmatic dependent of the up kernel.
-static int launch_down_cluster(const DownArgs &a, cudaStream_t st) {
-    const int epc = (a.K + DC_CL - 1) / DC_CL;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(DC_CL, DC_NCH, 1);
-    cfg.blockDim = dim3(DC_TPE * epc);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = DC_CL;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    if (cudaLaunchKernelEx(&cfg, decode_down_cluster_kernel, a) != cudaSuccess) return QMOE_ERR_LAUNCH;
-    return launch_status();
-}
-
-// The fused down step of the decode-step layer: the cluster form for K <= 32, else the arrival-counter form.
-static int launch_down_fused(const DownArgs &a, cudaStream_t st, int dev) {
-    if (a.K <= DC_MAXK) return launch_down_cluster(a, st);
-    return launch_down<true>(a, st, dev, true);
-}
-
 // CTAs per expert of the fused layer: the largest of 8, 7, 6, 4, 3, 2, 1 (2688 / S a multiple of 16) with S * K
 // CTAs fitting the SMs at once; 0 when K exceeds the SMs (the two-kernel form then runs).
 static int layer_split(int K, int sms) {
@@ -1231,7 +981,7 @@ int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslo
     UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
-    return launch_down_fused(da, st, dev);
+    return launch_down<true>(da, st, dev, true);
 }
 
 int qmoe_decode(const uint8_t *slots, int64_t slot_bytes, int64_t nslots, const int32_t *sidx, const float *s2,
@@ -1341,7 +1091,7 @@ int qmoe_decode_groups_static(const uint8_t *slots_up, int64_t slot_bytes, int64
     UpArgs ua{slots_up, slot_bytes, nslots, sidx, K, s2, x, x_dtype, h, gmask8, status, counters, DN_NCHUNK, tab};
     if (int e = launch_up(ua, st, dev, *di)) return e;
     DownArgs da{tab, h, gmask8, nullptr, nullptr, s2, coef, K, 1, part, gidx, gcnt, y, counters, status};
-    return launch_down_fused(da, st, dev);
+    return launch_down<true>(da, st, dev, true);
 }
 
 // The status word at the start of the static array: the first device-side error of the calls since it was last
