@@ -162,6 +162,15 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
                          const float *weights, const float *s2, const void *x, int x_dtype, int T, int topk, float *out,
                          void *workspace, size_t workspace_bytes, void *stream);
 
+/* No counterpart in the reference. Bound, in SM clock cycles, on each device-side wait of the kernels that wait
+ * (the pipeline roles of qmoe_prefill_grouped's tensor-core GEMMs) on the current device, from the next call on;
+ * cycles <= 0 restores the default of 4e9 cycles (about 2 s). A wait that runs out records QMOE_ERR_TIMEOUT in the
+ * workspace status word and the kernel stops: every copy it started lands and every MMA it issued completes
+ * (each waited for with the default bound) before it frees its tensor memory and returns; its outputs are then
+ * undefined and the next call runs normally. Meant for failure handling and its tests: a short bound makes
+ * ordinary calls time out. */
+int qmoe_set_wait_cycles(long long cycles);
+
 /* ------------------------------------------------------------------ expert parallelism */
 
 /* No counterpart in the reference (it runs every expert on one GPU). Expert e lives on rank

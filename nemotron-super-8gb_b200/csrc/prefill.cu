@@ -55,6 +55,7 @@ struct Params {
     int T, topk, P, nchunks, tiles_cap;
     float *out;             // [T, 1024] f32
     int *status;
+    long long wait_cycles;  // bound on each wait of the GEMM roles, in SM clock cycles
     int *tile_count;
     int *cnt;               // [ne]
     int *eoff;              // [ne + 1]
@@ -307,9 +308,20 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
 }
 
 
-__device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+// Bounded wait for the phase with the given parity: false after `limit` SM clock cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, long long limit) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > limit) return false;
+    }
+    return true;
+}
+
+__device__ __forceinline__ bool lane_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                          long long limit) {
     if (mbar_try_wait(bar, parity)) return true;   // ready: no need to look at the abort flag
-    const bool ok = !*abort_flag && mbar_wait(bar, parity);
+    const bool ok = !*abort_flag && mbar_wait_for(bar, parity, limit);
     if (!ok) {
         set_error(status, DEV_ERR_TIMEOUT);
         *abort_flag = 1;
@@ -361,7 +373,8 @@ struct BsPlan {
     static constexpr int NBAR = 4 * STAGES + 8;
     static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
     static constexpr int OFF_ABORT = OFF_TMEM + 16;
-    static constexpr int SMEM = OFF_ABORT + 16 + 1024;
+    static constexpr int OFF_REC = OFF_ABORT + 16;   // [STAGES][8] ints: the last use each role armed / arrived for
+    static constexpr int SMEM = OFF_REC + STAGES * 32 + 1024;
     static_assert(SMEM <= 232448, "fits the 227 KB opt-in");
     static_assert(SLAB % 16 == 0, "bulk copy size");
 };
@@ -576,19 +589,20 @@ __device__ __forceinline__ uint32_t instr_desc_nvfp4(int n) {
 // slot; warp 9 issues the MMAs into one of two TMEM accumulators while warps 0..3 drain the other (epilogue).
 // Waits of the producer and epilogue roles: between polls the thread sleeps, so that polling warps leave the
 // issue slots of their SM sub-partition to the MMA-issuing warp.
-__device__ __forceinline__ bool mbar_wait_bo(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bo(uint64_t *bar, uint32_t parity, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         __nanosleep(200);
-        if (clock64() - t0 > WAIT_CYCLES) return false;
+        if (clock64() - t0 > limit) return false;
     }
     return true;
 }
 
-__device__ __forceinline__ bool lane_wait_bo(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status) {
+__device__ __forceinline__ bool lane_wait_bo(uint64_t *bar, uint32_t parity, volatile int *abort_flag, int *status,
+                                             long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
-    const bool ok = !*abort_flag && mbar_wait_bo(bar, parity);
+    const bool ok = !*abort_flag && mbar_wait_bo(bar, parity, limit);
     if (!ok) {
         set_error(status, DEV_ERR_TIMEOUT);
         *abort_flag = 1;
@@ -597,9 +611,9 @@ __device__ __forceinline__ bool lane_wait_bo(uint64_t *bar, uint32_t parity, vol
 }
 
 __device__ __forceinline__ bool warp_wait_bo(uint64_t *bar, uint32_t parity, int lane, volatile int *abort_flag,
-                                             int *status) {
+                                             int *status, long long limit) {
     bool ok = true;
-    if (lane == 0) ok = lane_wait_bo(bar, parity, abort_flag, status);
+    if (lane == 0) ok = lane_wait_bo(bar, parity, abort_flag, status, limit);
     return __shfl_sync(0xffffffffu, ok, 0);
 }
 
@@ -629,8 +643,13 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     uint64_t *acc_empty = acc_full + 2;
     uint64_t *slab_full = acc_empty + 2;
     uint64_t *sf_src = slab_full + 2;    // [S] the stage's scale atoms are in shared memory (bulk copy + weight atoms)
+    uint64_t *mma_drain = sf_src + S;    // after an abort: every MMA issued has completed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sm + Plan::OFF_TMEM);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(sm + Plan::OFF_ABORT);
+    // rec[s][r]: the last use (running stage count q) of stage s that role r armed or arrived for: 0 the weight
+    // issuers (full, expect_tx), 1 the plane issuers (full and sf_src, expect_tx), 2 the weight-atom warp (sf_src),
+    // 3.. the scale-store warps (full). Read only after an abort, to let every copy in flight land before the exit.
+    int *rec = reinterpret_cast<int *>(sm + Plan::OFF_REC);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -646,7 +665,9 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             mbar_init(&acc_empty[a], 4);
             mbar_init(&slab_full[a], 1);
         }
+        mbar_init(mma_drain, 1);
         *abort_flag = 0;
+        for (int k = 0; k < S * 8; k++) rec[k] = -1;
         fence_mbar_init();
     }
     if (warp == BS_W_MMA) {
@@ -676,7 +697,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 for (int kt = 0; kt < nst; kt++, q++) {
                     if ((int)(q % BS_NA) != pr) continue;
                     const int s = q % S;
-                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
+                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status, p.wait_cycles)) {
                         ok = false;
                         break;
                     }
@@ -685,6 +706,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     for (int hh = 0; hh < nh; hh++)
                         tma_load_3d(sm + s * BS_STAGE + hh * BS_A, &tm_w, (k0 + hh) * (BS_BK / 2),
                                     (PH == PH_UP ? 0 : p.dn_row0) + mt * BM, e, &full[s]);
+                    atomicMax(&rec[s * 8 + 0], (int)q);
                 }
                 if (!ok) break;
             }
@@ -711,7 +733,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 for (int kt = 0; kt < nst; kt++, q++) {
                     if ((int)(q % BS_NB) != pb) continue;
                     const int s = q % S;
-                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status)) {
+                    if (!lane_wait_bo(&empty[s], ((q / S) & 1) ^ 1, abort_flag, p.status, p.wait_cycles)) {
                         ok = false;
                         break;
                     }
@@ -725,6 +747,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     for (int hh = 0; hh < nh; hh++)
                         tma_load_3d(st + (wide ? BW_B + hh * pbytes : BS_A), map, (k0 + hh) * (BS_BK / 2), n0, 0,
                                     &full[s]);
+                    atomicMax(&rec[s * 8 + 1], (int)q);
                 }
                 if (!ok) break;
             }
@@ -766,7 +789,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 }
                 issued[b ^ 1]++;
             }
-            if (!warp_wait_bo(&slab_full[b], (j >> 1) & 1, lane, abort_flag, p.status)) break;
+            if (!warp_wait_bo(&slab_full[b], (j >> 1) & 1, lane, abort_flag, p.status, p.wait_cycles)) break;
             mbar_try_wait(&slab_full[b], (j >> 1) & 1);   // completed phase: acquire for every lane
             done[b]++;
             const uint8_t *sl = slab + b * Plan::SLAB;
@@ -775,7 +798,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             bool ok = true;
             for (int kt = 0; kt < nst; kt++, q++) {
                 const int s = q % S;
-                if (!warp_wait_bo(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status)) {
+                if (!warp_wait_bo(&empty[s], ((q / S) & 1) ^ 1, lane, abort_flag, p.status, p.wait_cycles)) {
                     ok = false;
                     break;
                 }
@@ -791,7 +814,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 }
                 fence_async_smem();   // generic-proxy atom stores, ordered before the async proxy's next use
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&sf_src[s]);
+                if (lane == 0) {
+                    mbar_arrive(&sf_src[s]);
+                    rec[s * 8 + 2] = (int)q;
+                }
             }
             if (!ok) break;
         }
@@ -816,7 +842,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const int np_ = b_rows(n);
                 const bool fused = fused_planes(np_);
                 const int a = j & 1;
-                if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status)) break;
+                if (!lane_wait(&acc_empty[a], ((j >> 1) & 1) ^ 1, abort_flag, p.status, p.wait_cycles)) break;
                 tc_fence_after();
                 const uint32_t idesc = instr_desc_nvfp4(fused ? NP * np_ : (n + 15) & ~15);
                 const uint32_t d = tmem + a * NT;
@@ -824,7 +850,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const uint32_t pstride = (uint32_t)(np_ * (BS_BK / 2)) >> 4;   // one plane of B, in 16-byte units
                 bool ok = true;
                 for (int kt = 0; kt < nst; kt++) {
-                    if (!lane_wait(&full[s], ph, abort_flag, p.status)) {
+                    if (!lane_wait(&full[s], ph, abort_flag, p.status, p.wait_cycles)) {
                         ok = false;
                         break;
                     }
@@ -877,7 +903,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             bool ok = true;
             for (int kt = 0; kt < nst; kt++, q++) {
                 const int s = q % S;
-                if (!warp_wait_bo(&sf_src[s], (q / S) & 1, lane, abort_flag, p.status)) {
+                if (!warp_wait_bo(&sf_src[s], (q / S) & 1, lane, abort_flag, p.status, p.wait_cycles)) {
                     ok = false;
                     break;
                 }
@@ -901,7 +927,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[s]);
+                    if (lane == 0) {
+                        mbar_arrive(&full[s]);
+                        rec[s * 8 + 3 + (warp - BS_W_SS)] = (int)q;
+                    }
                     continue;
                 }
                 const uint8_t *at = sm + s * BS_STAGE + BS_A + BS_B;
@@ -920,7 +949,10 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[s]);
+                if (lane == 0) {
+                    mbar_arrive(&full[s]);
+                    rec[s * 8 + 3 + (warp - BS_W_SS)] = (int)q;
+                }
             }
             if (!ok) break;
         }
@@ -960,7 +992,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
             named_sync(1, 128);   // this item's column scales are visible; colsc[a ^ 1] is free
             const bool more = i + (int)gridDim.x < nitems;
             if (more) fetch(i + gridDim.x);
-            const bool acc_ok = warp_wait_bo(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status);
+            const bool acc_ok = warp_wait_bo(&acc_full[a], (j >> 1) & 1, lane, abort_flag, p.status, p.wait_cycles);
             tc_fence_after();
             const uint32_t trow = tmem + a * NT + ((uint32_t)(warp * 32) << 16);
             // a fused-plane tile holds plane pl of pair c in column pl * h + c: the pair's value is the sum
@@ -1030,9 +1062,41 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
     }
     tc_fence_before();
     __syncthreads();
+    const bool aborted = *abort_flag != 0;
     if (warp == BS_W_MMA) {
+        // after an abort an accumulator may not have been waited for (two commits to one acc_full barrier can
+        // then be pending, which a parity wait cannot tell apart): one more commit, on a barrier of its own,
+        // arrives once every MMA this thread issued has completed
+        if (aborted && lane == 0) {
+            mma_commit(mma_drain);
+            mbar_wait(mma_drain, 0);
+        }
+        __syncwarp();
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BS_TMEM_COLS) : "memory");
+    } else if (aborted && tid == 0) {
+        // After an abort, copies may still be in flight into stages whose barrier phase will never complete.
+        // Each stage has at most one pending phase per barrier (a producer arms use q + S only after the
+        // consumers released use q). Its use is the largest one any role recorded; the roles that have not
+        // arrived for it are arrived for here, so the phase completes exactly when the bytes still in flight
+        // have landed, and that completion is waited for (bounded) before the CTA's shared memory is released.
+        for (int s = 0; s < S; s++) {
+            const int *r = rec + s * 8;
+            int qf = r[0];   // full[s]: the weight issuers, the plane issuers, the scale-store warps
+            for (int k = 1; k < 3 + BS_NSS; k++)
+                if (k != 2) qf = max(qf, r[k]);
+            if (qf >= 0) {
+                for (int k = 0; k < 3 + BS_NSS; k++)
+                    if (k != 2 && r[k] < qf) mbar_arrive(&full[s]);
+                mbar_wait(&full[s], (uint32_t)(qf / S) & 1);
+            }
+            const int qs = max(r[1], r[2]);   // sf_src[s]: the plane issuers (atoms), the weight-atom warp
+            if (qs >= 0) {
+                if (r[1] < qs) mbar_arrive(&sf_src[s]);
+                if (r[2] < qs) mbar_arrive(&sf_src[s]);
+                mbar_wait(&sf_src[s], (uint32_t)(qs / S) & 1);
+            }
+        }
     }
 }
 
@@ -1213,6 +1277,7 @@ inline bool make_plane_map(CUtensorMap *m, void *base, int64_t P, int row_bytes,
 }
 
 std::atomic<uint64_t> g_smem_up{0}, g_smem_dn_o{0};
+std::atomic<long long> g_wait_cycles[MAX_DEVICES];   // 0: the default bound
 
 } // namespace pf
 } // namespace qmoe
@@ -1261,6 +1326,8 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     p.tiles_cap = L.tiles_cap;
     p.out = out;
     p.status = reinterpret_cast<int *>(ws + L.status);
+    const long long wc = g_wait_cycles[dev].load(std::memory_order_relaxed);
+    p.wait_cycles = wc > 0 ? wc : WAIT_CYCLES;
     p.tile_count = reinterpret_cast<int *>(ws + L.tile_count);
     p.cnt = reinterpret_cast<int *>(ws + L.cnt);
     p.eoff = reinterpret_cast<int *>(ws + L.eoff);
@@ -1333,6 +1400,14 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
     dn<<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
+}
+
+int qmoe_set_wait_cycles(long long cycles) {
+    int dev;
+    DeviceInfo *di;
+    if (int rc = current_device(&dev, &di)) return rc;
+    pf::g_wait_cycles[dev].store(cycles > 0 ? cycles : 0, std::memory_order_relaxed);
+    return QMOE_OK;
 }
 
 } // extern "C"

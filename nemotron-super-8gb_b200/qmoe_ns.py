@@ -196,6 +196,15 @@ def prefill_status(device=None, clear=True):
     return int(C.lib().qmoe_workspace_status(C.ptr(ws), int(clear), C.stream_of(ws)))
 
 
+def set_wait_cycles(cycles, device=None):
+    """Bound, in SM clock cycles, on each device-side wait of moe_prefill's GEMM pipelines on the device (the
+    current one by default), from the next call on; cycles <= 0 restores the default (4e9, about 2 s). A wait
+    that runs out records QMOE_ERR_TIMEOUT (prefill_status() == 4) and the kernel stops after its copies and
+    MMAs in flight complete. No counterpart in the reference."""
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        C.call("qmoe_set_wait_cycles", int(cycles))
+
+
 def moe_pairs_T(slots_u8, pslot, ptok, s2p, coefp, X, h_buf, out_buf):
     """qmoe_ns.py:318-324: pairs over T-layout slots. The slots used are converted to the orig layout
     in a scratch copy (from_T) and the pairs kernels run on it, as the reference engine's prompt path

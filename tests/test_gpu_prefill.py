@@ -180,3 +180,30 @@ def test_prefill_T_layout_in_cuda_graph(Q, bank):
     torch.cuda.synchronize()
     assert torch.equal(y_graph, y_eager)
     del g
+
+
+def test_prefill_wait_limit_times_out_and_recovers(Q, bank):
+    """qmoe_set_wait_cycles(300): a wait of the GEMM pipeline runs out long before its copies land, the call
+    records QMOE_ERR_TIMEOUT (4) in the workspace status, and the kernels stop after every copy and MMA in
+    flight has completed. With the default bound restored, the next call is clean and bit-identical to a
+    call made before the timeout (the context and the workspace stay usable)."""
+    b = bank
+    T, k = 48, 22
+    ids, w = _route(T, 24, k, seed=77)
+    idd, wd = torch.from_numpy(ids).to(DEV), torch.from_numpy(w).to(DEV)
+    y_ref = Q.moe_prefill(b["blkT"], idd, wd, b["s2"], b["X"][:T]).clone()
+    assert Q.prefill_status() == 0
+    seen = []
+    Q.set_wait_cycles(300)
+    try:
+        for _ in range(3):
+            Q.moe_prefill(b["blkT"], idd, wd, b["s2"], b["X"][:T])
+            seen.append(Q.prefill_status())
+            if seen[-1] == 4:
+                break
+    finally:
+        Q.set_wait_cycles(0)
+    assert seen[-1] == 4 and set(seen) <= {0, 4}, seen
+    y = Q.moe_prefill(b["blkT"], idd, wd, b["s2"], b["X"][:T])
+    assert Q.prefill_status() == 0
+    assert torch.equal(y, y_ref)
