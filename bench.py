@@ -41,10 +41,12 @@ sys.path.insert(0, os.path.join(ROOT, "nemotron-super-8gb_b200"))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE decode us/token (40-layer routed-expert decode, bs=1)"
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one decode_layer_kernel launch at K = 22, from a
-# single-launch ncu capture of this workload; ncu cannot run inside the timed bench, so the figure is carried here
-# (None until a capture of the current kernel is summarised)
-LAYER_TRAFFIC_NCU = None
+# One decode_layer_kernel launch at K = 22 from a single-launch ncu capture (`--layers 2` store, 13th launch):
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) and the bytes its loads moved from L2 to the SMs
+# (l1tex__m_xbar2l1tex_read_bytes.sum). That layer's live fraction is below the mean, so the line reports the
+# DRAM/requested ratio applied to the mean layer's algorithmic bytes. ncu cannot run inside the timed bench,
+# so the figures are carried here.
+LAYER_TRAFFIC_NCU = {"dram_bytes": 34996480, "requested_bytes": 35736640}
 N_LAYERS, NE, K = 40, 512, 22
 N_TOK = 64
 
@@ -1088,9 +1090,13 @@ def main():
             "bytes_per_token": int(bytes_per_token),
             "roofline": {"kernel": "decode_layer_kernel + decode_finish_kernel (one layer)", "bound": "hbm",
                          "achieved": round(layer_gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(layer_gbs / hbm, 4), "traffic": LAYER_TRAFFIC_NCU,
-                         "traffic_source": "ncu single-launch capture of decode_layer_kernel (DRAM read + write), "
-                                           "a 22-expert layer at the mean live fraction",
+                         "frac": round(layer_gbs / hbm, 4),
+                         "traffic": int(layer_bytes * LAYER_TRAFFIC_NCU["dram_bytes"] / LAYER_TRAFFIC_NCU["requested_bytes"]),
+                         "traffic_source": "ncu single-launch capture of decode_layer_kernel: DRAM read + write "
+                                           f"{LAYER_TRAFFIC_NCU['dram_bytes']} B against the "
+                                           f"{LAYER_TRAFFIC_NCU['requested_bytes']} B its loads requested from L2 "
+                                           "(a layer below the mean live fraction), the ratio scaled to this "
+                                           "line's mean layer",
                          "bytes_per_launch": int(layer_bytes), "us_per_launch": round(layer_us, 3)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/token", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h), "copies": "per layer: one H2D of its inputs, one D2H of y",
