@@ -597,6 +597,10 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
     const uint8_t *blk = reinterpret_cast<const uint8_t *>(a.tab[j]);
     const bool bad_tab = blk == nullptr || (reinterpret_cast<uintptr_t>(blk) & 15u) != 0;
 
+    // Each warp's first tile is requested before x is prepared, so that the two latencies overlap.
+    UpTile tn;
+    if (warp < ntile && !bad) up_load(base, n0 / UP_ROWS + warp, lane, tn);
+
     UpArgs xa{};
     xa.x = a.x;
     xa.x_dtype = a.x_dtype;
@@ -608,8 +612,6 @@ __global__ void __launch_bounds__(FL_THREADS, 1) decode_layer_kernel(LayerArgs a
     // ---- U: the CTA's up tiles (8 rows each), warp w takes tiles w, w+12, ..., the next tile's loads in flight
     {
         int t = warp;
-        UpTile tn;
-        if (t < ntile && !bad) up_load(base, n0 / UP_ROWS + t, lane, tn);
         for (; t < ntile; t += FL_NW) {
             const UpTile tc = tn;
             if (t + FL_NW < ntile && !bad) up_load(base, n0 / UP_ROWS + t + FL_NW, lane, tn);
