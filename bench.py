@@ -1004,11 +1004,13 @@ def main():
     hbm, peak_kind = peaks()
     layer_gbs = layer_bytes / (layer_us * 1e-6) / 1e9
 
-    # ---- e2e through the public path with host buffers, layer by layer as the model runs it: per layer one H2D
-    # copy of that layer's packed routed inputs (x, slot ids, block addresses, s2, weights) from pinned host memory,
-    # the layer's qmoe_decode_groups call, and one D2H copy of its output y, each layer after the previous one's
-    # output is back (layer m+1's input depends on layer m's output). The 40-layer sequence is one CUDA graph; two
-    # pinned staging records alternate, each refilled on the host for the next token once its last replay is done.
+    # ---- e2e through the public path with host buffers, layer by layer as the model runs it: per layer the layer's
+    # packed routed inputs (x, slot ids, block addresses, s2, weights) cross from pinned host memory
+    # (qmoe_copy_async: a kernel chained after the previous layer's last kernel), the layer's qmoe_decode_groups
+    # call runs, and its output y goes straight back into pinned host memory (the finish kernel's stores), each
+    # layer after the previous one's output is back (layer m+1's input depends on layer m's output). The 40-layer
+    # sequence is one CUDA graph; two pinned staging records alternate, each refilled on the host for the next
+    # token once its last replay is done.
     REC = 2048 + K * (4 + 8 + 8 + 4)   # x bf16 | sidx i32 | tab i64 | s2 f32 x2 | coef f32
     offs = {"X": 0, "SIDX": 2048, "TAB": 2048 + 4 * K, "S2": 2048 + 12 * K, "W": 2048 + 20 * K}
     host_all = torch.empty(N_TOK, L, REC, dtype=torch.uint8)
@@ -1023,20 +1025,20 @@ def main():
         return rec_dev[m, offs[k_]:offs[k_] + n * torch.tensor([], dtype=dt).element_size()].view(dt)
 
     fn = C.lib().qmoe_decode_groups
+    cp = C.lib().qmoe_copy_async
     g_e2e = []
     for b in range(2):
         stage[b].copy_(host_all[0])
         gph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gph, stream=stream):
             for m in range(L):
-                rec_dev[m].copy_(stage[b][m], non_blocking=True)
+                assert cp(rec_dev[m].data_ptr(), stage[b][m].data_ptr(), REC, stream.cuda_stream) == 0
                 rc = fn(store.data_ptr(), store.stride(0), store.shape[0], view("SIDX", m, torch.int32, K).data_ptr(),
                         view("TAB", m, torch.int64, K).data_ptr(), view("S2", m, torch.float32, 2 * K).data_ptr(),
                         view("W", m, torch.float32, K).data_ptr(), view("X", m, torch.bfloat16, S.LAT).data_ptr(), 1, K,
                         step.h[m].data_ptr(), step.gidx[m].data_ptr(), step.gcnt[m].data_ptr(), step.part[m].data_ptr(),
-                        step.Y[m].data_ptr(), step.ws.data_ptr(), step.ws.numel(), stream.cuda_stream)
+                        y_host[b][m].data_ptr(), step.ws.data_ptr(), step.ws.numel(), stream.cuda_stream)
                 assert rc == 0
-                y_host[b][m].copy_(step.Y[m], non_blocking=True)
         g_e2e.append(gph)
     done = [torch.cuda.Event(), torch.cuda.Event()]
     h2d = L * REC
@@ -1099,7 +1101,8 @@ def main():
                                            "line's mean layer",
                          "bytes_per_launch": int(layer_bytes), "us_per_launch": round(layer_us, 3)},
             "e2e": {"value": round(e2e_us, 3), "unit": "us/token", "h2d_bytes_per_step": int(h2d),
-                    "d2h_bytes_per_step": int(d2h), "copies": "per layer: one H2D of its inputs, one D2H of y",
+                    "d2h_bytes_per_step": int(d2h), "copies": "per layer: its packed inputs read from pinned host memory by a chained copy kernel "
+                             "(qmoe_copy_async), y written by the layer's finish kernel into pinned host memory",
                     "matches_device_path": e2e_ok},
             "gpu_launches": 2 * L * args.steps,
             "clocks": clocks,

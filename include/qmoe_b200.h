@@ -58,6 +58,14 @@ const char *qmoe_status_string(int status);
  * Returns QMOE_OK or the first device-side error code the kernels recorded; `clear` resets it. */
 int qmoe_workspace_status(void *workspace, int clear, void *stream);
 
+/* No counterpart in the reference (its host round trips are torch copies). Copies `bytes` from src to dst with a
+ * kernel launched as a programmatic dependent of the preceding kernel on `stream`: for the small per-layer records
+ * of a decode step whose inputs come from the host (x, routing) and whose output goes back (y), inside the kernel
+ * chain rather than as copy-engine transfers between kernels. Either pointer may be pinned host memory
+ * (cudaHostAlloc / torch pin_memory: device-accessible under unified addressing); regions must not overlap.
+ * bytes == 0 does nothing. */
+int qmoe_copy_async(void *dst, const void *src, size_t bytes, void *stream);
+
 /* ------------------------------------------------------------------ routed experts, decode step */
 
 /* Replaces `_up` (qmoe_ns.py:24-44) as launched by moe_decode / moe_decode_groups
@@ -91,7 +99,8 @@ int qmoe_decode_down_groups(const int64_t *tab, const float *h, const int32_t *g
  * neurons' down rows) and a small kernel summing the experts in slot order; above it, the up GEMV and the
  * live-group down GEMV. Both launch as programmatic dependents of the preceding work on `stream`. The
  * workspace (size from qmoe_decode_groups_workspace_bytes, zero-filled once) must not be used by another
- * call running concurrently. */
+ * call running concurrently. y may be pinned host memory (device-accessible under unified addressing): the
+ * finish kernel then writes the layer's output straight back to the host. */
 size_t qmoe_decode_groups_workspace_bytes(int K);
 int qmoe_decode_groups(const uint8_t *slots_up, int64_t slot_bytes, int64_t nslots, const int32_t *sidx,
                        const int64_t *tab,

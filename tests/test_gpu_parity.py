@@ -467,3 +467,43 @@ def test_decode_groups_graph_capture_and_determinism(Q, experts, oracle_decode):
     for o in outs:
         assert torch.equal(o, y0)      # bit-identical replays
     assert rel_l2(y0.cpu().numpy(), oracle_decode[0]) < FP32_TOL
+
+
+def test_copy_async_and_decode_with_host_y(Q, experts):
+    """qmoe_copy_async moves small records between pinned host memory and the device inside the kernel chain
+    (16-byte words with odd tails, and bytes when an end is unaligned) and writes nothing outside the range;
+    qmoe_decode_groups with y in pinned host memory (the per-layer host round trip of the bench's e2e leg,
+    inputs staged by qmoe_copy_async) gives the device-resident result bit for bit."""
+    import _qmoe_lib as C
+    lib = C.lib()
+    st = torch.cuda.current_stream().cuda_stream
+    g = torch.Generator().manual_seed(5)
+    for n, soff, doff in ((1, 0, 0), (15, 0, 0), (2576, 0, 0), (100003, 0, 0), (4099, 3, 1), (64, 16, 5)):
+        src = torch.randint(0, 256, (n + soff,), dtype=torch.uint8, generator=g).pin_memory()
+        dev = torch.zeros(n + 32, dtype=torch.uint8, device=DEV)
+        back = torch.zeros(n, dtype=torch.uint8).pin_memory()
+        assert lib.qmoe_copy_async(dev.data_ptr() + doff, src.data_ptr() + soff, n, st) == 0
+        assert lib.qmoe_copy_async(back.data_ptr(), dev.data_ptr() + doff, n, st) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(back, src[soff:])
+        assert int(dev[:doff].sum()) == 0 and int(dev[doff + n:].sum()) == 0
+    assert lib.qmoe_copy_async(0, 0, 0, st) == 0              # nothing to do
+    assert lib.qmoe_copy_async(0, src.data_ptr(), 8, st) == 5  # QMOE_ERR_NULL
+
+    e = experts
+    K = 22
+    T, tab, b = _T_setup(Q, e)
+    sidx = torch.arange(K, dtype=torch.int32, device=DEV)
+    y_dev = Q.moe_decode_groups(T, sidx, tab, e["s2"], e["coef"], e["x"], b["h"], b["part"], b["gidx"], b["gcnt"])
+    x_host = e["x"].cpu().pin_memory()
+    x_dev = torch.empty_like(e["x"])
+    y_host = torch.full((Q.LAT,), float("nan")).pin_memory()
+    ws = torch.zeros(int(lib.qmoe_decode_groups_workspace_bytes(K)), dtype=torch.uint8, device=DEV)
+    assert lib.qmoe_copy_async(x_dev.data_ptr(), x_host.data_ptr(), x_host.numel() * 2, st) == 0
+    rc = lib.qmoe_decode_groups(T.data_ptr(), T.stride(0), T.shape[0], sidx.data_ptr(), tab.data_ptr(),
+                                e["s2"].data_ptr(), e["coef"].data_ptr(), x_dev.data_ptr(), C.dtype_code(x_dev), K,
+                                b["h"].data_ptr(), b["gidx"].data_ptr(), b["gcnt"].data_ptr(), b["part"].data_ptr(),
+                                y_host.data_ptr(), ws.data_ptr(), ws.numel(), st)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y_host, y_dev.cpu())
