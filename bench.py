@@ -356,6 +356,10 @@ def run_reference(args):
             samples.append(dt * 1e6)
         if time.perf_counter() - t_all > 240:   # a bound on the whole run; the line reports the steps timed
             break
+    if not samples:
+        print(json.dumps({"impl": "reference", "unavailable": "the warm-up steps used up the 240 s bound of the "
+                          "CPU path; run with fewer warm-up steps"}), flush=True)
+        return
     v = float(np.mean(samples))
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 1), "unit": "us/token", "n_gpus": args.gpus,
             "steps": len(samples), "warmup": args.warmup, "ms_per_step": round(v / 1e3, 3), "higher_is_better": False,
