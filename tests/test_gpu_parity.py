@@ -507,3 +507,60 @@ def test_copy_async_and_decode_with_host_y(Q, experts):
     assert rc == 0
     torch.cuda.synchronize()
     assert torch.equal(y_host, y_dev.cpu())
+
+
+@pytest.mark.parametrize("xdt", [torch.float16, torch.float32])
+def test_activation_dtypes(Q, D, synth, experts, xdt):
+    """f16 and fp32 activations (the other two x dtypes of the C ABI) through the decode layer (the fused kernel
+    at K = 22 and the two-kernel path at K = 150; fp32 activations run separate kernel instantiations that keep
+    x in fp32), the prefill grouped GEMM, and the FP8 / NVFP4 GEMVs, each against the fp64 oracle evaluated on the
+    very values passed in."""
+    e = experts
+    g = synth.seeded(77, DEV)
+    x = e["x"].float()
+    if xdt == torch.float32:
+        x = x + 1e-3 * torch.randn(x.shape, generator=g, device=DEV)   # values bf16 and f16 cannot hold
+    x = x.to(xdt)
+    x_np = x.float().cpu().numpy()
+    T, tab, _ = _T_setup(Q, e)
+    for K in (22, 150):
+        idx = torch.arange(K, device=DEV) % 22
+        coef = (torch.rand(K, generator=g, device=DEV) + 0.1).contiguous()
+        h = torch.empty(K, Q.INTER, device=DEV)
+        part = torch.empty(2, K, Q.LAT, device=DEV)
+        gidx = torch.empty(K, 168, dtype=torch.int32, device=DEV)
+        gcnt = torch.empty(K, dtype=torch.int32, device=DEV)
+        y = Q.moe_decode_groups(T, idx.to(torch.int32).contiguous(), tab[idx].contiguous(), e["s2"][idx].contiguous(),
+                                coef, x, h, part, gidx, gcnt)
+        ii = idx.cpu().numpy()
+        y64, _, _ = O.moe_decode([e["blk_np"][i] for i in ii], e["s2_np"][ii], coef.cpu().numpy(), x_np)
+        assert rel_l2(y.cpu().numpy(), y64) < FP32_TOL, (K, rel_l2(y.cpu().numpy(), y64))
+
+    # prefill: 8 tokens (scaled copies of x) routed to 6 of the 22 orig-layout experts each
+    Tt, k = 8, 6
+    rng = np.random.default_rng(3)
+    ids = np.stack([rng.permutation(22)[:k] for _ in range(Tt)]).astype(np.int32)
+    w = rng.uniform(0.1, 1.0, (Tt, k)).astype(np.float32)
+    X = torch.stack([x.float() * (0.5 + 0.15 * i) for i in range(Tt)]).to(xdt)
+    yp = Q.moe_prefill(e["blk"], torch.from_numpy(ids).to(DEV), torch.from_numpy(w).to(DEV), e["s2"], X,
+                       layout_T=False)
+    pslot = ids.reshape(-1)
+    ptok = np.repeat(np.arange(Tt, dtype=np.int32), k)
+    ref = O.pairs(list(e["blk_np"]), pslot, ptok, e["s2_np"][pslot], w.reshape(-1), X.float().cpu().numpy())
+    assert rel_l2(yp.cpu().numpy(), ref.reshape(Tt, k, -1).sum(1)) < 2.0 ** -8
+    assert Q.prefill_status() == 0
+
+    # dense GEMVs at M = 1
+    for fmt, N, Kd in (("fp8", 4096, 4096), ("nvfp4", 2688, 4096)):
+        wf = torch.randn(N, Kd, generator=g, device=DEV) * 0.02
+        if fmt == "fp8":
+            codes, s = synth.quantize_fp8(wf)
+            q = {"fmt": "fp8", "w": codes, "s": s.to(DEV), "N": N, "K": Kd}
+            sc_np = None
+        else:
+            codes, sc, s2 = synth.quantize_nvfp4(wf)
+            q = {"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2.reshape(1), "N": N, "K": Kd}
+            sc_np = sc.cpu().numpy()
+        xv = torch.randn(Kd, generator=g, device=DEV).to(xdt)
+        ref = O.dense(fmt, q["w"].cpu().numpy(), sc_np, float(q["s"]), N, Kd, xv.float().cpu().numpy()[None])[0]
+        assert rel_l2(D.gemv(q, xv).cpu().numpy(), ref) < FP32_TOL, fmt
