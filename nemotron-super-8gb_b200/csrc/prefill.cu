@@ -387,8 +387,15 @@ constexpr int BS_TMEM_COLS = 512;                     // accumulators at 0 and N
 constexpr int BS_SF_COL = 2 * NT;                     // 2*NT + 32 s (per k-step: 4 columns SFA, 4 per plane)
 static_assert(BS_SF_COL + 32 * 5 <= BS_TMEM_COLS && BS_KS * (1 + NP) * 4 <= 32, "TMEM plan");
 
-// Pair rows loaded for a tile of n pairs (the TMA box heights).
-__device__ __forceinline__ int b_rows(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : n <= 64 ? 64 : 128; }
+// Pair rows loaded for a tile of n pairs (the TMA box heights): 16 or 32 for the fused-plane tiles, else n
+// rounded up to a multiple of 16, so that a tile reads at most 15 rows of planes it does not use.
+__host__ __device__ __forceinline__ int b_rows(int n) { return n <= 16 ? 16 : n <= 32 ? 32 : (n + 15) & ~15; }
+constexpr int NBOX = NT / 16;   // box heights 16, 32, ..., NT
+
+// The plane tensor maps of one GEMM, one per box height (16 * (k + 1) rows).
+struct PlaneMaps {
+    CUtensorMap m[NBOX];
+};
 
 // 16 fp32 values -> NP NVFP4 planes: codes[p] = 8 bytes (element 2i in the low nibble of byte i), scale
 // byte sc[p] (e4m3, round to nearest; the e2m1 codes saturate, the residual carries the difference).
@@ -619,9 +626,7 @@ __device__ __forceinline__ bool warp_wait_bo(uint64_t *bar, uint32_t parity, int
 
 template <int PH>
 __global__ void __launch_bounds__(BS_THREADS, 1)
-    pfb_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b16,
-                    const __grid_constant__ CUtensorMap tm_b32, const __grid_constant__ CUtensorMap tm_b64,
-                    const __grid_constant__ CUtensorMap tm_b128) {
+    pfb_gemm_kernel(const Params p, const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ PlaneMaps tm_b) {
     constexpr int MT = PH == PH_UP ? MT_UP : MT_DN;
     constexpr int K = PH == PH_UP ? LAT : INTER;
     constexpr int NST = K / BS_BK;                     // stages per item
@@ -724,7 +729,7 @@ __global__ void __launch_bounds__(BS_THREADS, 1)
                 const int4 td = td_next;
                 if (i + (int)gridDim.x < nitems) td_next = p.tiles[(i + gridDim.x) / MT];
                 const int n0 = td.y, np_ = b_rows(td.z);
-                const CUtensorMap *map = np_ == 16 ? &tm_b16 : np_ == 32 ? &tm_b32 : np_ == 64 ? &tm_b64 : &tm_b128;
+                const CUtensorMap *map = &tm_b.m[(np_ >> 4) - 1];
                 const uint8_t *sfb_tile = sfb + (int64_t)(i / MT) * KS * NP * BS_ATOM;
                 const bool wide = fused_planes(np_);
                 const int nst = wide ? (NST + 1) / 2 : NST;
@@ -1366,10 +1371,11 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
 
     // both halves: block-scaled NVFP4 on the weights as stored (the down half of a T-layout store converted
     // first), the activations as NVFP4 planes
-    const int hts[4] = {16, 32, 64, 128};
-    CUtensorMap xm[4], hm[4], wu, wdo;
-    for (int k = 0; k < 4; k++) {
-        if (!make_plane_map(&xm[k], p.xq, L.P, LAT / 2, hts[k]) || !make_plane_map(&hm[k], p.hq, L.P, KB_DN, hts[k]))
+    PlaneMaps xm, hm;
+    CUtensorMap wu, wdo;
+    for (int k = 0; k < NBOX; k++) {
+        if (!make_plane_map(&xm.m[k], p.xq, L.P, LAT / 2, 16 * (k + 1)) ||
+            !make_plane_map(&hm.m[k], p.hq, L.P, KB_DN, 16 * (k + 1)))
             return QMOE_ERR_LAUNCH;
     }
     if (!make_store_map(&wu, store, block_stride, n_experts, KB_UP, BS_BK / 2, BM, CU_TENSOR_MAP_SWIZZLE_64B))
@@ -1395,9 +1401,9 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
         pf_dnT_codes_kernel<<<dim3(INTER / DCV_R, LAT / 256, n_experts), 256, 0, st>>>(p);
         pf_dnT_scales_kernel<<<dim3(LAT / DCV_C, n_experts), 256, 0, st>>>(p);
     }
-    up<<<di->sms, BS_THREADS, BsPlan<PH_UP>::SMEM, st>>>(p, wu, xm[0], xm[1], xm[2], xm[3]);
+    up<<<di->sms, BS_THREADS, BsPlan<PH_UP>::SMEM, st>>>(p, wu, xm);
     pf_hplanes_kernel<<<(L.P + 7) / 8, 256, 0, st>>>(p);
-    dn<<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm[0], hm[1], hm[2], hm[3]);
+    dn<<<di->sms, BS_THREADS, BsPlan<PH_DN_O>::SMEM, st>>>(p, wdo, hm);
     pf_combine_kernel<<<T, 256, 0, st>>>(p);
     return launch_status();
 }
