@@ -360,11 +360,11 @@ static_assert(BW_SFA + 2 * BS_SFA == BS_STAGE && BW_B % 512 == 0 && (NP * 16 * (
               "a wide stage fills the stage; its plane halves start on 64-byte swizzle atoms");
 
 // Shared-memory plan of pfb_gemm_kernel<PH>: the stage ring, two slabs of the item's weight scales (128 rows
-// x all of K: 8 KB up, 21 KB down), epilogue staging, barriers. The down half's larger slabs leave room for
-// four stages, the up half has five.
+// x all of K: 8 KB up, 21 KB down), epilogue staging, barriers: five stages for both halves (the down half's
+// five stages and two 21 KB slabs take 224 KB of the 227 KB opt-in).
 template <int PH>
 struct BsPlan {
-    static constexpr int STAGES = PH == PH_UP ? 5 : 4;
+    static constexpr int STAGES = 5;
     static constexpr int SLAB = BM * (PH == PH_UP ? G_UP : G_DN);
     static constexpr int OFF_SLAB = STAGES * BS_STAGE;
     static constexpr int OFF_COLSC = OFF_SLAB + 2 * SLAB;
