@@ -69,6 +69,16 @@ def test_no_gpu_means_device_error(L):
     fake = ctypes.c_void_p(16)
     # valid arguments, no CUDA device: the device check refuses (no fallback path exists)
     assert lib.qmoe_decode_up(fake, 1548288, 1, fake, 22, fake, fake, 1, fake, None) == 7
+    assert lib.qmoe_copy_async(fake, fake, 64, None) == 7
+    assert lib.qmoe_set_wait_cycles(300) == 7
+
+
+def test_copy_async_argument_checks_need_no_gpu(L):
+    lib = L.lib()
+    fake = ctypes.c_void_p(16)
+    assert lib.qmoe_copy_async(None, None, 0, None) == 0     # nothing to copy: no CUDA call at all
+    assert lib.qmoe_copy_async(None, fake, 8, None) == 5     # QMOE_ERR_NULL
+    assert lib.qmoe_copy_async(fake, None, 8, None) == 5
 
 
 def test_python_mirror_refuses_cpu_tensors(L):
