@@ -207,3 +207,32 @@ def test_prefill_wait_limit_times_out_and_recovers(Q, bank):
     y = Q.moe_prefill(b["blkT"], idd, wd, b["s2"], b["X"][:T])
     assert Q.prefill_status() == 0
     assert torch.equal(y, y_ref)
+
+
+def test_prefill_every_box_height(Q, bank):
+    """Tiles of 1, 15, 16, 17, 31, 32, 33, 40, 47, 48, 49, 63, 64, 65, 79, 80, 81, 95, 96, 97, 111, 112, 113, 127
+    and 128 pairs (one expert each, k = 1): every plane box height (16, 32, then 48 ... 128 rows), every MMA
+    width, the fused-plane and the per-plane MMAs, in both layouts, each token against the fp64 oracle."""
+    b = bank
+    sizes = [1, 15, 16, 17, 31, 32, 33, 40, 47, 48, 49, 63, 64, 65, 79, 80, 81, 95, 96, 97, 111, 112, 113, 127]
+    sizes = sizes + [128]                       # the 25th size goes to expert 0 again: a second tile of it
+    experts = [i % 24 for i in range(len(sizes))]
+    ids = np.concatenate([np.full(n, e, dtype=np.int32) for n, e in zip(sizes, experts)])[:, None]
+    T = ids.shape[0]
+    rng = np.random.default_rng(11)
+    perm = rng.permutation(T)                   # tokens of one expert spread over the prompt
+    ids = ids[perm]
+    w = rng.uniform(0.1, 1.0, (T, 1)).astype(np.float32)
+    g = torch.Generator(device=DEV)
+    g.manual_seed(9)
+    X = (b["X"].repeat(T // 48 + 1, 1)[:T].float() * (1 + 0.1 * torch.rand(T, 1, generator=g, device=DEV))).to(torch.bfloat16)
+    ref = oracle_prefill(b["blk_np"], b["s2_np"], ids, w, X.float().cpu().numpy())
+    outs = []
+    for layout_T, store in ((True, b["blkT"]), (False, b["blk"])):
+        y = Q.moe_prefill(store, torch.from_numpy(ids).to(DEV), torch.from_numpy(w).to(DEV), b["s2"], X,
+                          layout_T=layout_T)
+        assert Q.prefill_status() == 0
+        yn = y.cpu().numpy()
+        assert max(rel_l2(yn[t], ref[t]) for t in range(T)) < BF16_TOL
+        outs.append(y)
+    assert torch.equal(outs[0], outs[1])
