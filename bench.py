@@ -59,7 +59,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=N_LAYERS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "dense", "prefill", "ep"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "dense", "prefill", "ep", "decode_step"])
     ap.add_argument("--ep-t", type=int, default=64, help="ep workload: tokens per rank per step (config 4 decode batch)")
     ap.add_argument("--prefill-t", type=int, default=2048, help="prefill workload: tokens per call (config 3)")
     ap.add_argument("--prefill-layout", default="orig", choices=["orig", "T"],
@@ -747,6 +747,87 @@ def prefill_record(args, T, layout_T=False, steps=None, warmup=None, cpu=True, e
     return rec
 
 
+def run_decode_step(args):
+    """--workload decode_step: the whole decode-step MoE block of every layer, one token through all layers in
+    order as one CUDA graph (decode_step.DecodeGraph over decode_step.MoELayer: the router over the 4096-wide
+    hidden state, the bf16 latent projections 4096 -> 1024 and 1024 -> 4096 as in the reference
+    (nem_super.py:358-392), the 512 routed NVFP4 experts of config 1's store, the NVFP4 shared expert 2688 x 4096
+    / 4096 x 2688), each layer's output feeding the next. value: us/token over K tokens rotating over 64 (inputs
+    resident in HBM); the routed bytes are counted from the live groups and neurons each layer recorded for the
+    tokens; the dense bytes are the layer weights. Synthetic weights: the live fractions follow from random
+    projections, not config 1's recipe, and are reported."""
+    import numpy as np
+    import torch
+    import decode_step as DS
+    import expert_store as ES
+    import qmoe_synth as S
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    L, H, SI = args.layers, 4096, 2688
+    store, s2, _, _, _ = build_store(torch, S, dev, L, seed=1000, layout_T=True)
+    est = ES.ExpertStore.from_tensors(store, s2, "T")
+    g = S.seeded(616, dev)
+
+    def nvfp4(n, k):
+        codes, sc, s2_ = S.quantize_nvfp4(torch.randn(n, k, generator=g, device=dev) * 0.02)
+        return {"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2_.float().reshape(1), "N": n, "K": k}
+
+    layers, dense_bytes = [], 0
+    for m in range(L):
+        gate = (torch.randn(NE, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        bias = torch.randn(NE, generator=g, device=dev) * 0.01
+        fc1 = (torch.randn(S.LAT, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        fc2 = (torch.randn(H, S.LAT, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        layers.append(DS.MoELayer(m, est, gate, bias, fc1, fc2, nvfp4(SI, H), nvfp4(H, SI)))
+        dense_bytes += 2 * (gate.numel() + fc1.numel() + fc2.numel()) + 2 * (SI * H // 2 + SI * H // 16)
+    graph = DS.DecodeGraph(layers, H, device=dev)
+    xs = torch.randn(N_TOK, H, generator=g, device=dev).to(torch.bfloat16)
+    for i in range(max(3, args.warmup)):
+        graph.replay(xs[i % N_TOK])
+    torch.cuda.synchronize()
+    clk = Clocks(0)
+    clk.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        graph.replay(xs[(args.warmup + i) % N_TOK])
+    e1.record()
+    e1.synchronize()
+    clocks = clk.stop()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    routed, live = [], []
+    for t in range(4):   # the bytes the routed experts read for a few tokens, from what each layer recorded
+        graph.replay(xs[t])
+        torch.cuda.synchronize()
+        b = n = 0
+        for lay in layers:
+            ex = lay.experts
+            b += K * S.O_DW + 1024 * int(ex.gcnt.sum()) + 512 * int((ex.h > 0).sum())   # O_DW = the up half (UPB)
+            n += int((ex.h > 0).sum())
+        routed.append(b)
+        live.append(n / (L * K * S.INTER))
+    bytes_per_token = float(np.mean(routed)) + dense_bytes
+    hbm, peak_kind = peaks()
+    gbs = bytes_per_token / (us * 1e-6) / 1e9
+    line = {"metric": "MoE decode-step us/token (whole MoE block: router, latent projections, routed and shared "
+                      "experts, 40 layers, bs=1)", "value": round(us, 3), "unit": "us/token", "n_gpus": 1,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(us / 1e3, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4/bf16 -> f32",
+            "data": "synthetic",
+            "config": {"workload": "decode step: whole MoE block per layer, one CUDA graph per token", "layers": L,
+                       "hidden": H, "experts": NE, "top_k": K, "tokens_rotated": N_TOK},
+            "live_fraction": round(float(np.mean(live)), 4), "bytes_per_token": int(bytes_per_token),
+            "dense_bytes_per_token": int(dense_bytes),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "traffic": None},
+            "gpu_launches": 4 * L * args.steps,
+            "gpu_launches_note": "libqmoe_b200 kernels (layer, finish, two shared-expert GEMVs per layer); torch's "
+                                 "router, top-k and bf16 linears are not counted",
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill(args):
     """--workload prefill: the prefill record of --prefill-t tokens as the line."""
     rec = prefill_record(args, args.prefill_t, layout_T=args.prefill_layout == "T")
@@ -925,6 +1006,8 @@ def main():
         return run_ep(args)
     if args.workload == "dense":
         return run_dense(args)
+    if args.workload == "decode_step":
+        return run_decode_step(args)
     import torch
     import torch.distributed as dist
 

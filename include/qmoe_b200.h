@@ -180,6 +180,19 @@ int qmoe_prefill_grouped(const uint8_t *store, int64_t block_stride, int n_exper
  * ordinary calls time out. */
 int qmoe_set_wait_cycles(long long cycles);
 
+/* Replaces, for a decode step (one token), the routing of NemotronHTopkRouter.forward / route_tokens_to_experts
+ * (tf:697-720, 748-751; the reference calls it at nem_super.py:366-367) after its fp32 linear, together with the
+ * expert-store lookup of the routed layer: from logits [n_experts] f32 (the router's fp32 linear) and the
+ * correction bias [n_experts] f32, score = sigmoid(logit), choice = score + bias, the top_k largest choices (ties
+ * to the lower id; a NaN choice is never taken), weight = score * scaling (no renormalisation: norm_topk_prob
+ * false, one expert group). For each chosen expert r (in order of decreasing choice): ids[r] its id,
+ * sidx[r] = slot_base + id its store row, tab[r] = blocks + sidx[r] * block_stride, s2_sel[r] = s2[id] (two
+ * f32), coef[r] its weight. The sets of ids and weights are those of the reference; their order is not (the
+ * reference's top-k is unsorted). 1 <= top_k <= 32, top_k <= n_experts <= 1024. */
+int qmoe_route_decode(const float *logits, const float *bias, int n_experts, int top_k, float scaling, int slot_base,
+                      const uint8_t *blocks, int64_t block_stride, const float *s2, int64_t *ids, int32_t *sidx,
+                      int64_t *tab, float *s2_sel, float *coef, void *stream);
+
 /* ------------------------------------------------------------------ expert parallelism */
 
 /* No counterpart in the reference (it runs every expert on one GPU). Expert e lives on rank

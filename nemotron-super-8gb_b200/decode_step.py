@@ -12,12 +12,16 @@ NemotronHMoE.forward (tf:722-737) over device-side parts:
     out = fc2_latent_proj(y) + shared_down(relu(shared_up(x))^2) (dense_q GEMVs)
 
 `MoELayer.forward` runs it eagerly; `DecodeGraph` records the layers of a step once as a CUDA graph over
-static input/output buffers and replays it per token (one launch for the whole step).
+static input/output buffers and replays it per token (one launch for the whole step). For one token on a
+T-layout store, everything after the router's fp32 linear (sigmoid, bias, top-k, weights and the store
+lookup of the chosen experts) is one kernel (qmoe_route_decode) instead of a dozen small torch launches.
 """
 import torch
 import torch.nn.functional as F
 
+import _qmoe_lib as C
 import dense_q as D
+import qmoe_ns as Q
 from expert_store import RoutedExperts
 
 
@@ -58,18 +62,45 @@ class MoELayer(torch.nn.Module):
     def __init__(self, m, store, gate_w, bias, fc1, fc2, shared_up, shared_down, top_k=22, scaling=5.0,
                  n_group=1, topk_group=1, norm_topk_prob=False):
         super().__init__()
-        self.gate_w, self.bias = gate_w, bias
+        self.gate_w = gate_w.to(torch.float32).contiguous()   # the router computes in fp32: convert once (exact)
+        self.bias = bias.to(torch.float32).contiguous()
         self.fc1, self.fc2, self.shared_up, self.shared_down = fc1, fc2, shared_up, shared_down
         self.route_args = dict(top_k=top_k, scaling=scaling, n_group=n_group, topk_group=topk_group,
                                norm_topk_prob=norm_topk_prob)
         self.experts = RoutedExperts(m, store, topk=top_k)
+        # one-token routing in one kernel (one expert group, no renormalisation, a T-layout store)
+        self.fused = n_group == 1 and not norm_topk_prob and store.layout == "T" and gate_w.shape[0] <= 1024
+        if self.fused:
+            dev = store.device
+            self.r_ids = torch.empty(top_k, dtype=torch.int64, device=dev)
+            self.r_sidx = torch.empty(top_k, dtype=torch.int32, device=dev)
+            self.r_tab = torch.empty(top_k, dtype=torch.int64, device=dev)
+            self.r_s2 = torch.empty(top_k, 2, dtype=torch.float32, device=dev)
+            self.r_coef = torch.empty(top_k, dtype=torch.float32, device=dev)
+
+    def route_decode(self, x):
+        """One token: the router's fp32 linear, then qmoe_route_decode. Returns (ids, weights, store rows,
+        block addresses, s2 rows) of the chosen experts, in order of decreasing choice."""
+        st, ex = self.experts.store, self.experts
+        logits = F.linear(x.to(torch.float32), self.gate_w).contiguous()
+        C.call("qmoe_route_decode", C.ptr(logits), C.ptr(self.bias), self.gate_w.shape[0], self.route_args["top_k"],
+               float(self.route_args["scaling"]), ex.i * st.e_local - st.lo, C.ptr(st.blocks), int(st.blocks.stride(0)),
+               C.ptr(st.s2[ex.i]), C.ptr(self.r_ids), C.ptr(self.r_sidx), C.ptr(self.r_tab), C.ptr(self.r_s2),
+               C.ptr(self.r_coef), C.stream_of(logits))
+        return self.r_ids, self.r_coef, self.r_sidx, self.r_tab, self.r_s2
 
     def forward(self, hidden_states):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
-        ids, w = route_tokens(x, self.gate_w, self.bias, **self.route_args)
         lat = linear(self.fc1, x)
-        y = self.experts(lat, ids, w)
+        if self.fused and x.shape[0] == 1:
+            _, coef, sidx, tab, s2 = self.route_decode(x)
+            ex = self.experts
+            y = Q.moe_decode_groups(ex.store.blocks, sidx, tab, s2, coef, lat[0], ex.h, ex.part, ex.gidx, ex.gcnt)
+            y = y.view(1, -1).to(lat.dtype)
+        else:
+            ids, w = route_tokens(x, self.gate_w, self.bias, **self.route_args)
+            y = self.experts(lat, ids, w)
         out = linear(self.fc2, y)
         u = torch.relu(linear(self.shared_up, x))
         out = out + linear(self.shared_down, u * u)

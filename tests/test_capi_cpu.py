@@ -73,6 +73,16 @@ def test_no_gpu_means_device_error(L):
     assert lib.qmoe_set_wait_cycles(300) == 7
 
 
+def test_route_decode_argument_checks_need_no_gpu(L):
+    lib = L.lib()
+    f = ctypes.c_void_p(16)
+    args = lambda ne, k: (f, f, ne, k, 5.0, 0, f, 3096576, f, f, f, f, f, f, None)
+    assert lib.qmoe_route_decode(None, *args(512, 22)[1:]) == 5      # QMOE_ERR_NULL
+    assert lib.qmoe_route_decode(*args(512, 33)) == 1                # top_k > 32
+    assert lib.qmoe_route_decode(*args(1025, 22)) == 1               # n_experts > 1024
+    assert lib.qmoe_route_decode(*args(16, 22)) == 1                 # top_k > n_experts
+
+
 def test_copy_async_argument_checks_need_no_gpu(L):
     lib = L.lib()
     fake = ctypes.c_void_p(16)

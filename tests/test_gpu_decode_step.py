@@ -118,3 +118,27 @@ def test_step_graph_equals_eager(model):
         got = graph.replay(x).clone()
         torch.cuda.synchronize()
         assert rel_l2(got.float().cpu().numpy(), h.float().cpu().numpy()) < 1e-6
+
+
+def test_fused_routing_matches_torch_routing(model):
+    """qmoe_route_decode (one token: sigmoid, bias, top-22, weights and the store lookup in one kernel) against
+    the torch routing (tf:697-720, 748-751) on the same fp32 logits: the same 22 experts with bit-identical
+    weights, in order of decreasing choice; store rows, block addresses and s2 rows are those of the chosen
+    experts. The torch routing stays the reference and the path for grouped or batched routing."""
+    import decode_step as DS
+    for m, layer in enumerate(model["layers"]):
+        assert layer.fused
+        st, ex = layer.experts.store, layer.experts
+        for t in range(8):
+            x = torch.randn(1, H, generator=model["g"], device=DEV).to(torch.bfloat16)
+            ids_t, w_t = DS.route_tokens(x, layer.gate_w, layer.bias)
+            ids, coef, sidx, tab, s2 = (a.clone() for a in layer.route_decode(x))
+            ref = dict(zip(ids_t[0].tolist(), w_t[0].tolist()))
+            got = dict(zip(ids.tolist(), coef.tolist()))
+            assert set(got) == set(ref) and len(ids.unique()) == K
+            assert all(got[e] == ref[e] for e in ref)                      # bit-identical weights
+            choice = torch.nn.functional.linear(x.float(), layer.gate_w)[0].sigmoid() + layer.bias
+            assert torch.all(choice[ids][:-1] >= choice[ids][1:])          # decreasing choice
+            assert torch.equal(sidx, st.slot_index(ex.i, ids))
+            assert torch.equal(tab, st.block_addresses(sidx))
+            assert torch.equal(s2, st.s2[ex.i][ids])
