@@ -242,6 +242,14 @@ int dq_gemv_fp8(const uint8_t *w, const float *s, const void *x, int x_dtype, in
 int dq_gemv_nvfp4(const uint8_t *w, const uint8_t *sc, const float *s2, const void *x, int x_dtype, int M, int N,
                   int K, float *y, void *stream);
 
+/* The same GEMV with a bf16 result that folds in the bf16 operators that follow it in the model's shared expert
+ * (tf:722-737: shared_experts(x) = down(relu(up(x))^2), added to the routed output), with torch's roundings:
+ * epilogue 0: y = bf16(v) (as dense_q.qlinear returns); 1: y = bf16(relu(bf16(v))^2) (the up projection and its
+ * squared ReLU); 2: y = bf16(bf16(v) + residual) (the down projection added to residual [M, N] bf16). v is
+ * dq_gemv_nvfp4's fp32 result, so each epilogue equals the unfused torch sequence bit for bit. y [M, N] bf16. */
+int dq_gemv_nvfp4_bf16(const uint8_t *w, const uint8_t *sc, const float *s2, const void *x, int x_dtype, int M, int N,
+                       int K, int epilogue, const uint16_t *residual, uint16_t *y, void *stream);
+
 /* Replaces `dequant_rows` (dense_q.py:179-188): rows [r0, r1) (r1 <= N) of a quantized weight -> out [r1-r0, K]
  * (FP8: e4m3 * s; NVFP4: e2m1 * (e4m3 * s2), computed in fp32 and rounded to out_dtype, a QMOE_DT_*
  * code), bit-exact with the reference. fmt 0 = FP8, 1 = NVFP4; sc ignored for FP8. */

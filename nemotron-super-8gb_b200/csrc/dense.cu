@@ -127,6 +127,30 @@ int dq_gemv_nvfp4(const uint8_t *w, const uint8_t *sc, const float *s2, const vo
     return launch_dense<1>(g, as_stream(stream), dev, *di);
 }
 
+int dq_gemv_nvfp4_bf16(const uint8_t *w, const uint8_t *sc, const float *s2, const void *x, int x_dtype, int M, int N,
+                       int K, int epilogue, const uint16_t *residual, uint16_t *y, void *stream) {
+    if (!w || !sc || !s2 || !x || !y || (epilogue == 2 && !residual)) return QMOE_ERR_NULL;
+    if (epilogue < 0 || epilogue > 2 || M < 1 || M > 4 || N < 1 || K < 32 || (K % 32)) return QMOE_ERR_SHAPE;
+    if (!aligned16(w) || (reinterpret_cast<uintptr_t>(sc) & 1u)) return QMOE_ERR_ALIGN;
+    if (!valid_dtype(x_dtype)) return QMOE_ERR_DTYPE;
+    int dev;
+    DeviceInfo *di;
+    if (int e = current_device(&dev, &di)) return e;
+    GemvArgs g{};
+    g.w = w;
+    g.sc = sc;
+    g.s = s2;
+    g.x = x;
+    g.x_dtype = x_dtype;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.out_op = epilogue == 0 ? 3 : epilogue;   // 3: the plain bf16 cast (neither 1 nor 2 below)
+    g.ybf = y;
+    g.res = residual;
+    return launch_dense<1>(g, as_stream(stream), dev, *di);
+}
+
 int dq_dequant_rows(int fmt, const uint8_t *w, const uint8_t *sc, const float *s, int64_t N, int64_t K, int64_t r0,
                     int64_t r1, void *out, int out_dtype, void *stream) {
     if (!w || !s || !out || (fmt == 1 && !sc)) return QMOE_ERR_NULL;

@@ -41,6 +41,11 @@ struct GemvArgs {
     const float *coef;    // [items]
     const float *hin;     // down modes: f32 vectors [items, K]
     float *hout;          // pair up: h out [items, N]
+    // dense, bf16 output instead of y: 1 = bf16 of relu(bf16(v))^2, 2 = bf16 of bf16(v) + res, 3 = bf16(v)
+    // (torch's roundings); 0 = the fp32 y
+    int out_op;
+    uint16_t *ybf;
+    const uint16_t *res;
 };
 
 constexpr int GEMV_THREADS = 256;
@@ -250,7 +255,21 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
             for (int m = 0; m < M; ++m) {
                 const float v = (lane == 0 ? acc[0][m] : acc[1][m]) * inv[m];
                 if (MODE == GM_DENSE) {
-                    a.y[(int64_t)m * a.N + row] = v * mult;
+                    const int64_t o = (int64_t)m * a.N + row;
+                    if (a.out_op == 0) {
+                        a.y[o] = v * mult;
+                    } else {
+                        // the linear's output as torch leaves it (bf16), then relu^2 or the residual add, each
+                        // computed in fp32 and rounded to bf16 as torch's bf16 operators do
+                        float b = __bfloat162float(__float2bfloat16_rn(v * mult));
+                        if (a.out_op == 1) {
+                            b = b > 0.f ? b : (b != b ? b : 0.f);   // relu, NaN kept
+                            b = b * b;
+                        } else if (a.out_op == 2) {
+                            b = b + __bfloat162float(__ushort_as_bfloat16(a.res[o]));
+                        }   // 3: the bf16 cast alone
+                        a.ybf[o] = __bfloat16_as_ushort(__float2bfloat16_rn(b));
+                    }
                 } else if (MODE == GM_PAIR_UP) {
                     float u = v * mult;
                     u = fmaxf(u, 0.f);

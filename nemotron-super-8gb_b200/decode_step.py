@@ -102,9 +102,27 @@ class MoELayer(torch.nn.Module):
             ids, w = route_tokens(x, self.gate_w, self.bias, **self.route_args)
             y = self.experts(lat, ids, w)
         out = linear(self.fc2, y)
+        if self._fused_shared(x, out):
+            su, sd = self.shared_up, self.shared_down
+            u2 = torch.empty(1, su["N"], dtype=torch.bfloat16, device=x.device)
+            res = torch.empty_like(out)
+            st = C.stream_of(x)
+            C.call("dq_gemv_nvfp4_bf16", C.ptr(su["w"]), C.ptr(su["sc"]), C.ptr(su["s"]), C.ptr(x), C.dtype_code(x),
+                   1, su["N"], su["K"], 1, None, C.ptr(u2), st)
+            C.call("dq_gemv_nvfp4_bf16", C.ptr(sd["w"]), C.ptr(sd["sc"]), C.ptr(sd["s"]), C.ptr(u2), C.dtype_code(u2),
+                   1, sd["N"], sd["K"], 2, C.ptr(out), C.ptr(res), st)
+            return res.view(shape)
         u = torch.relu(linear(self.shared_up, x))
         out = out + linear(self.shared_down, u * u)
         return out.view(shape)
+
+    def _fused_shared(self, x, out):
+        """One token, bf16 hidden states, an NVFP4 shared expert: its up projection with the squared ReLU and its
+        down projection with the add are one GEMV each (dq_gemv_nvfp4_bf16; bit-identical to the torch ops)."""
+        su, sd = self.shared_up, self.shared_down
+        return (x.shape[0] == 1 and x.dtype == torch.bfloat16 and out.dtype == torch.bfloat16
+                and isinstance(su, dict) and isinstance(sd, dict) and su["fmt"] == "nvfp4" and sd["fmt"] == "nvfp4"
+                and out.is_contiguous() and x.is_contiguous())
 
 
 class DecodeGraph:

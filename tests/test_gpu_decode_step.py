@@ -142,3 +142,19 @@ def test_fused_routing_matches_torch_routing(model):
             assert torch.equal(sidx, st.slot_index(ex.i, ids))
             assert torch.equal(tab, st.block_addresses(sidx))
             assert torch.equal(s2, st.s2[ex.i][ids])
+
+
+def test_fused_shared_expert_is_bit_identical(model):
+    """The shared expert through dq_gemv_nvfp4_bf16 (up projection with its squared ReLU, down projection with
+    the add onto the routed output) equals the unfused torch sequence (qlinear, relu, square, qlinear, add)
+    bit for bit, for the whole layer."""
+    layer = model["layers"][0]
+    for t in range(3):
+        x = torch.randn(1, H, generator=model["g"], device=DEV).to(torch.bfloat16)
+        fused = layer(x).clone()
+        layer._fused_shared = lambda *a: False
+        try:
+            plain = layer(x).clone()
+        finally:
+            del layer._fused_shared
+        assert torch.equal(fused, plain)

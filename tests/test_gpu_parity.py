@@ -564,3 +564,24 @@ def test_activation_dtypes(Q, D, synth, experts, xdt):
         xv = torch.randn(Kd, generator=g, device=DEV).to(xdt)
         ref = O.dense(fmt, q["w"].cpu().numpy(), sc_np, float(q["s"]), N, Kd, xv.float().cpu().numpy()[None])[0]
         assert rel_l2(D.gemv(q, xv).cpu().numpy(), ref) < FP32_TOL, fmt
+
+
+def test_nvfp4_gemv_bf16_epilogues(D, synth):
+    """dq_gemv_nvfp4_bf16: the bf16 cast, bf16(relu(bf16(v))^2) and bf16(bf16(v) + residual) equal torch's bf16
+    operators applied to dq_gemv_nvfp4's fp32 result, bit for bit (M = 1 and 2)."""
+    import _qmoe_lib as C
+    g = synth.seeded(808, DEV)
+    N, K = 2688, 4096
+    codes, sc, s2 = synth.quantize_nvfp4(torch.randn(N, K, generator=g, device=DEV) * 0.02)
+    q = {"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2.reshape(1), "N": N, "K": K}
+    for M in (1, 2):
+        x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+        v = D.gemv_mb(q, x) if M > 1 else D.gemv(q, x[0]).view(1, N)
+        res = torch.randn(M, N, generator=g, device=DEV).to(torch.bfloat16)
+        u = torch.relu(v.to(torch.bfloat16))
+        expect = {0: v.to(torch.bfloat16), 1: u * u, 2: v.to(torch.bfloat16) + res}
+        for ep in (0, 1, 2):
+            y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+            C.call("dq_gemv_nvfp4_bf16", C.ptr(codes), C.ptr(sc), C.ptr(q["s"]), C.ptr(x), C.dtype_code(x), M, N, K,
+                   ep, C.ptr(res) if ep == 2 else None, C.ptr(y), C.stream_of(x))
+            assert torch.equal(y, expect[ep]), (M, ep)
