@@ -68,6 +68,7 @@ class MoELayer(torch.nn.Module):
         self.route_args = dict(top_k=top_k, scaling=scaling, n_group=n_group, topk_group=topk_group,
                                norm_topk_prob=norm_topk_prob)
         self.experts = RoutedExperts(m, store, topk=top_k)
+        self._side = {}   # device index -> side stream of the one-token path
         # one-token routing in one kernel (one expert group, no renormalisation, a T-layout store)
         self.fused = n_group == 1 and not norm_topk_prob and store.layout == "T" and gate_w.shape[0] <= 1024
         if self.fused:
@@ -92,6 +93,8 @@ class MoELayer(torch.nn.Module):
     def forward(self, hidden_states):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
+        if self.fused and x.shape[0] == 1 and self._fused_shared(x, x):
+            return self._forward_token(x).view(shape)
         lat = linear(self.fc1, x)
         if self.fused and x.shape[0] == 1:
             _, coef, sidx, tab, s2 = self.route_decode(x)
@@ -115,6 +118,40 @@ class MoELayer(torch.nn.Module):
         u = torch.relu(linear(self.shared_up, x))
         out = out + linear(self.shared_down, u * u)
         return out.view(shape)
+
+    def _forward_token(self, x):
+        """One token with every fused part: the latent projection fc1 and the whole shared expert (up projection
+        with its squared ReLU, down projection, each rounded to bf16 as the torch operators do) run on a side
+        stream, forked from and joined back to the caller's stream (a CUDA graph records them as a parallel
+        branch), while the router's linear, the routing kernel, the routed experts and fc2 run on the caller's
+        stream; the two results are added in bf16 at the end, as the unfused layer adds them."""
+        cur = torch.cuda.current_stream(x.device)
+        side = self._side.get(x.device.index)
+        if side is None:
+            side = self._side[x.device.index] = torch.cuda.Stream(x.device)
+        su, sd = self.shared_up, self.shared_down
+        side.wait_stream(cur)
+        with torch.cuda.stream(side):
+            lat = linear(self.fc1, x)
+            lat_ready = torch.cuda.Event()
+            lat_ready.record(side)
+            u2 = torch.empty(1, su["N"], dtype=torch.bfloat16, device=x.device)
+            C.call("dq_gemv_nvfp4_bf16", C.ptr(su["w"]), C.ptr(su["sc"]), C.ptr(su["s"]), C.ptr(x), C.dtype_code(x),
+                   1, su["N"], su["K"], 1, None, C.ptr(u2), side.cuda_stream)
+            shared = torch.empty(1, sd["N"], dtype=torch.bfloat16, device=x.device)
+            C.call("dq_gemv_nvfp4_bf16", C.ptr(sd["w"]), C.ptr(sd["sc"]), C.ptr(sd["s"]), C.ptr(u2), C.dtype_code(u2),
+                   1, sd["N"], sd["K"], 0, None, C.ptr(shared), side.cuda_stream)
+        _, coef, sidx, tab, s2 = self.route_decode(x)
+        cur.wait_event(lat_ready)
+        ex = self.experts
+        y = Q.moe_decode_groups(ex.store.blocks, sidx, tab, s2, coef, lat[0], ex.h, ex.part, ex.gidx, ex.gcnt)
+        out = linear(self.fc2, y.view(1, -1).to(lat.dtype))
+        cur.wait_stream(side)
+        if not torch.cuda.is_current_stream_capturing():   # made on the side stream, read on this one
+            lat.record_stream(cur)
+            u2.record_stream(cur)
+            shared.record_stream(cur)
+        return out + shared
 
     def _fused_shared(self, x, out):
         """One token, bf16 hidden states, an NVFP4 shared expert: its up projection with the squared ReLU and its
