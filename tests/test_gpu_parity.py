@@ -585,3 +585,43 @@ def test_nvfp4_gemv_bf16_epilogues(D, synth):
             C.call("dq_gemv_nvfp4_bf16", C.ptr(codes), C.ptr(sc), C.ptr(q["s"]), C.ptr(x), C.dtype_code(x), M, N, K,
                    ep, C.ptr(res) if ep == 2 else None, C.ptr(y), C.stream_of(x))
             assert torch.equal(y, expect[ep]), (M, ep)
+
+
+@pytest.mark.parametrize("ne,k", [(37, 5), (512, 1), (512, 22), (512, 32), (1024, 22)])
+def test_route_decode_shapes_and_ties(ne, k):
+    """qmoe_route_decode on random fp32 logits for expert counts that are not multiples of 32 and the limits
+    (1024 experts, top-32): the chosen set and its weights are those of torch (sigmoid, + bias, top-k, x scaling),
+    the order is by decreasing choice, and the store rows, block addresses and s2 rows follow the slot base.
+    Equal choices go to the lower expert id."""
+    import _qmoe_lib as C
+    g = torch.Generator(device=DEV).manual_seed(ne * 100 + k)
+    logits = torch.randn(ne, generator=g, device=DEV) * 3
+    bias = torch.randn(ne, generator=g, device=DEV) * 0.01
+    s2 = torch.rand(ne, 2, generator=g, device=DEV)
+    blocks = torch.empty(4, 64, dtype=torch.uint8, device=DEV)      # only addresses are formed from it
+    outs = dict(ids=torch.empty(k, dtype=torch.int64, device=DEV), sidx=torch.empty(k, dtype=torch.int32, device=DEV),
+                tab=torch.empty(k, dtype=torch.int64, device=DEV), s2=torch.empty(k, 2, device=DEV),
+                coef=torch.empty(k, device=DEV))
+
+    def run(lg):
+        C.call("qmoe_route_decode", C.ptr(lg), C.ptr(bias), ne, k, 2.5, 7, C.ptr(blocks), 1000, C.ptr(s2),
+               C.ptr(outs["ids"]), C.ptr(outs["sidx"]), C.ptr(outs["tab"]), C.ptr(outs["s2"]), C.ptr(outs["coef"]),
+               C.stream_of(lg))
+        torch.cuda.synchronize()
+        return {n: t.clone() for n, t in outs.items()}
+
+    o = run(logits)
+    score = logits.sigmoid()
+    choice = score + bias
+    ref = torch.topk(choice, k, sorted=False)[1]
+    assert set(o["ids"].tolist()) == set(ref.tolist())
+    assert torch.equal(o["coef"], score[o["ids"]] * 2.5)
+    assert torch.all(choice[o["ids"]][:-1] >= choice[o["ids"]][1:])
+    assert torch.equal(o["sidx"], (o["ids"] + 7).to(torch.int32))
+    assert torch.equal(o["tab"], blocks.data_ptr() + (o["ids"] + 7) * 1000)
+    assert torch.equal(o["s2"], s2[o["ids"]])
+    # ties: every logit equal and no bias -> the k lowest ids, in order
+    flat = torch.zeros(ne, device=DEV)
+    bias.zero_()
+    o = run(flat)
+    assert o["ids"].tolist() == list(range(k))
