@@ -688,24 +688,51 @@ def prefill_record(args, T, layout_T=False, steps=None, warmup=None, cpu=True, e
         clocks = clk.stop()
         ms = e0.elapsed_time(e1) / steps
         ms_e2e, ee = None, max(5, steps // 2)
-        if e2e:   # host inputs (pinned) -> device, call, output -> host, every step
+        if e2e:
+            # every step: the prompt's tokens and routing from pinned host memory to the device, the call, and its
+            # output back to pinned host memory. Prompts are independent, so as in a serving loop the copies run on
+            # an upload and a download stream beside the calls: step i+1's upload and step i-1's download overlap
+            # step i's call (double-buffered, each buffer reused only after the step that last used it is done).
             hx = X.cpu().pin_memory()
             hid = ids.cpu().pin_memory()
             hw = w.cpu().pin_memory()
-            hout = torch.empty(T, S.LAT, dtype=torch.float32).pin_memory()
-            dx, did, dw = torch.empty_like(X), torch.empty_like(ids), torch.empty_like(w)
+            hout = [torch.empty(T, S.LAT, dtype=torch.float32).pin_memory() for _ in range(2)]
+            dx = [torch.empty_like(X) for _ in range(2)]
+            did = [torch.empty_like(ids) for _ in range(2)]
+            dw = [torch.empty_like(w) for _ in range(2)]
+            dout = [torch.empty_like(out) for _ in range(2)]
+            us, ds = torch.cuda.Stream(), torch.cuda.Stream()
+            up = [torch.cuda.Event() for _ in range(2)]
+            done = [torch.cuda.Event() for _ in range(2)]
+            down = [torch.cuda.Event() for _ in range(2)]
             e2 = torch.cuda.Event(enable_timing=True)
             e3 = torch.cuda.Event(enable_timing=True)
             e2.record(st)
-            for _ in range(ee):
-                dx.copy_(hx, non_blocking=True)
-                did.copy_(hid, non_blocking=True)
-                dw.copy_(hw, non_blocking=True)
-                Q.moe_prefill(store, did, dw, s2l, dx, layout_T=layout_T, out=out)
-                hout.copy_(out, non_blocking=True)
+            us.wait_event(e2)
+            for i in range(ee):
+                b = i & 1
+                if i >= 2:
+                    us.wait_event(done[b])      # step i-2 has read this input set
+                with torch.cuda.stream(us):
+                    dx[b].copy_(hx, non_blocking=True)
+                    did[b].copy_(hid, non_blocking=True)
+                    dw[b].copy_(hw, non_blocking=True)
+                    up[b].record(us)
+                st.wait_event(up[b])
+                if i >= 2:
+                    st.wait_event(down[b])      # step i-2's output has left this buffer
+                Q.moe_prefill(store, did[b], dw[b], s2l, dx[b], layout_T=layout_T, out=dout[b])
+                done[b].record(st)
+                ds.wait_event(done[b])
+                with torch.cuda.stream(ds):
+                    hout[b].copy_(dout[b], non_blocking=True)
+                    down[b].record(ds)
+            st.wait_stream(us)
+            st.wait_stream(ds)
             e3.record(st)
             e3.synchronize()
             ms_e2e = e2.elapsed_time(e3) / ee
+            assert torch.equal(hout[(ee - 1) & 1], out.cpu())   # the last output back equals the device run's
     flop = T * K * PREFILL_FLOP_PER_PAIR
     wbytes = uniq * S.BLOCK
     act_bytes = T * S.LAT * 2 + T * S.LAT * 4 + T * K * 8
@@ -731,7 +758,9 @@ def prefill_record(args, T, layout_T=False, steps=None, warmup=None, cpu=True, e
     if ms_e2e is not None:
         rec["e2e"] = {"value": round(T / ms_e2e * 1e3, 1), "unit": "tokens/s",
                       "h2d_bytes_per_step": int(X.numel() * 2 + ids.numel() * 4 + w.numel() * 4),
-                      "d2h_bytes_per_step": int(out.numel() * 4)}
+                      "d2h_bytes_per_step": int(out.numel() * 4),
+                      "copies": "every step: its tokens and routing up from pinned host memory, its output back; "
+                                "on upload and download streams beside the calls (independent prompts, double-buffered)"}
     if cpu and not args.no_cpu_baseline:
         from oracle import oracle as O
         sh = s2l.cpu().numpy()
