@@ -968,22 +968,49 @@ def ep_record(args, world, rank, local, batches=((64, "decode_batch"), (8192, "p
         dist.all_reduce(pt, op=dist.ReduceOp.MAX)
         ph = {p: round(float(v), 4) for p, v in zip(EP_PHASES, pt.tolist())}
         tot = sum(ph.values())
-        # e2e through the public module: host token blocks + routing in, host outputs back, every layer
+        # e2e through the public module: host token blocks + routing in, host outputs back, every layer. The
+        # layers' blocks here are independent, so the copies run on an upload and a download stream beside the
+        # forwards: the next layer's upload and the previous layer's download overlap this layer's forward
+        # (inputs double-buffered; each output is read back from its own tensor).
         hX = [x.cpu().pin_memory() for x in X]
         hI = [r[0].cpu().pin_memory() for r in R]
         hW = [r[1].cpu().pin_memory() for r in R]
         hO = torch.empty(L, T, S.LAT, dtype=torch.float32).pin_memory()
+        dX = [torch.empty_like(X[0]) for _ in range(2)]
+        dI = [torch.empty_like(R[0][0]) for _ in range(2)]
+        dW = [torch.empty_like(R[0][1]) for _ in range(2)]
+        us, ds = torch.cuda.Stream(), torch.cuda.Stream()
+        up = [torch.cuda.Event() for _ in range(2)]
+        used = [torch.cuda.Event() for _ in range(2)]
         ee = max(2, steps // 2)
         dist.barrier()
         torch.cuda.synchronize()
+        cur = torch.cuda.current_stream()
         e2 = torch.cuda.Event(enable_timing=True)
         e3 = torch.cuda.Event(enable_timing=True)
         e2.record()
+        us.wait_event(e2)
+        q = 0
         for _ in range(ee):
             for m in range(L):
-                y = moe[m](hX[m].to(dev, non_blocking=True), hI[m].to(dev, non_blocking=True),
-                           hW[m].to(dev, non_blocking=True))
-                hO[m].copy_(y, non_blocking=True)
+                b = q & 1
+                if q >= 2:
+                    us.wait_event(used[b])       # the forward two layers back has read this input set
+                with torch.cuda.stream(us):
+                    dX[b].copy_(hX[m], non_blocking=True)
+                    dI[b].copy_(hI[m], non_blocking=True)
+                    dW[b].copy_(hW[m], non_blocking=True)
+                    up[b].record(us)
+                cur.wait_event(up[b])
+                y = moe[m](dX[b], dI[b], dW[b])
+                used[b].record(cur)
+                ds.wait_stream(cur)
+                y.record_stream(ds)
+                with torch.cuda.stream(ds):
+                    hO[m].copy_(y, non_blocking=True)
+                q += 1
+        cur.wait_stream(us)
+        cur.wait_stream(ds)
         e3.record()
         e3.synchronize()
         me = torch.tensor([e2.elapsed_time(e3) / ee], device=dev)
