@@ -818,11 +818,13 @@ def run_decode_step(args):
     clk.start()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()   # a profiler started with collection off (ncu --profile-from-start off) begins here
     e0.record()
     for i in range(args.steps):
         graph.replay(xs[(args.warmup + i) % N_TOK])
     e1.record()
     e1.synchronize()
+    torch.cuda.profiler.stop()
     clocks = clk.stop()
     us = e0.elapsed_time(e1) * 1e3 / args.steps
     routed, live = [], []

@@ -4,8 +4,9 @@
 // more (slot ids, block addresses, s2 rows); in a decode step each is a separate launch of a few microseconds.
 // Here the router logits still come from the caller's fp32 linear (so they are the reference's own), and this
 // kernel does the rest: score = sigmoid(logit) (expf, IEEE division, as torch's fp32 sigmoid), choice = score +
-// bias, the top_k choices (ties to the lower expert id), weight = score * scaling, and for each chosen expert its
-// store slot, block address and s2 row.
+// bias, the top_k choices (ties to the lower expert id; each expert's rank among all choices is counted in
+// parallel, so no sequential selection rounds), weight = score * scaling, and for each chosen expert its store slot,
+// block address and s2 row.
 #include <climits>
 #include <cmath>
 
@@ -24,10 +25,9 @@ __global__ void __launch_bounds__(RT_MAX_E) route_decode_kernel(const float *__r
                                                                  int64_t *ids, int32_t *sidx, int64_t *tab,
                                                                  float *s2_sel, float *coef) {
     __shared__ float score[RT_MAX_E];
-    __shared__ float wbest[32];
-    __shared__ int wbesti[32];
+    __shared__ __align__(16) float choice[RT_MAX_E];
     __shared__ int sel[RT_MAX_K];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int tid = threadIdx.x;
     float c = -INFINITY;
     if (tid < ne) {
         const float s = 1.f / (1.f + expf(-logits[tid]));
@@ -35,32 +35,22 @@ __global__ void __launch_bounds__(RT_MAX_E) route_decode_kernel(const float *__r
         c = s + bias[tid];
         if (c != c) c = -INFINITY;   // a NaN choice is never taken (torch.topk would rank it first)
     }
-    for (int r = 0; r < topk; ++r) {
-        // block arg-max of (choice, -id): the largest choice, ties to the lower expert id
-        float v = c;
-        int i = tid < ne ? tid : INT_MAX;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-            const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
-            if (v2 > v || (v2 == v && i2 < i)) v = v2, i = i2;
+    if (tid < ne) choice[tid] = c;
+    __syncthreads();
+    // rank of this expert = the experts whose choice beats it (larger, or equal with a lower id): a unique
+    // position in the order of decreasing choice, so the top_k need no sequential selection rounds
+    if (tid < ne) {
+        int rank = 0;
+        const int n4 = ne & ~3;
+        for (int j = 0; j < n4; j += 4) {
+            const float4 v = *reinterpret_cast<const float4 *>(choice + j);
+            rank += (v.x > c || (v.x == c && j < tid)) + (v.y > c || (v.y == c && j + 1 < tid)) +
+                    (v.z > c || (v.z == c && j + 2 < tid)) + (v.w > c || (v.w == c && j + 3 < tid));
         }
-        if (lane == 0) wbest[warp] = v, wbesti[warp] = i;
-        __syncthreads();
-        if (warp == 0) {
-            v = lane < nw ? wbest[lane] : -INFINITY;
-            i = lane < nw ? wbesti[lane] : INT_MAX;
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-                const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-                const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
-                if (v2 > v || (v2 == v && i2 < i)) v = v2, i = i2;
-            }
-            if (lane == 0) sel[r] = i;
-        }
-        __syncthreads();
-        if (tid == sel[r]) c = -INFINITY;   // taken
+        for (int j = n4; j < ne; ++j) rank += choice[j] > c || (choice[j] == c && j < tid);
+        if (rank < topk) sel[rank] = tid;
     }
+    __syncthreads();
     if (tid < topk) {
         const int e = sel[tid];
         const int slot = slot_base + e;
