@@ -242,6 +242,14 @@ int dq_gemv_fp8(const uint8_t *w, const float *s, const void *x, int x_dtype, in
 int dq_gemv_nvfp4(const uint8_t *w, const uint8_t *sc, const float *s2, const void *x, int x_dtype, int M, int N,
                   int K, float *y, void *stream);
 
+/* No counterpart kernel in the reference (its bf16 projections, e.g. fc1_latent_proj / fc2_latent_proj of the MoE
+ * block, nem_super.py:376-377, run through torch's F.linear): y [M, N] bf16 = bf16 weights w [N, K] times x [M, K]
+ * (bf16, f16 or fp32), the weights widened to fp32 exactly and every product accumulated in fp32, then rounded to
+ * bf16 with the same epilogues as dq_gemv_nvfp4_bf16 (0: the result; 1: relu^2; 2: + residual). 1 <= M <= 4,
+ * K % 8 == 0, w 16-byte aligned. */
+int dq_gemv_bf16(const uint16_t *w, const void *x, int x_dtype, int M, int N, int K, int epilogue,
+                 const uint16_t *residual, uint16_t *y, void *stream);
+
 /* The same GEMV with a bf16 result that folds in the bf16 operators that follow it in the model's shared expert
  * (tf:722-737: shared_experts(x) = down(relu(up(x))^2), added to the routed output), with torch's roundings:
  * epilogue 0: y = bf16(v) (as dense_q.qlinear returns); 1: y = bf16(relu(bf16(v))^2) (the up projection and its

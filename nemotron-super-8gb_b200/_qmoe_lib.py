@@ -37,6 +37,7 @@ SIGNATURES = {
     "qmoe_pairs": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p]),
     "qmoe_set_wait_cycles": (_i, [_c.c_longlong]),
     "qmoe_copy_async": (_i, [_p, _p, _sz, _p]),
+    "dq_gemv_bf16": (_i, [_p, _p, _i, _i, _i, _i, _i, _p, _p, _p]),
     "dq_gemv_nvfp4_bf16": (_i, [_p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p]),
     "qmoe_route_decode": (_i, [_p, _p, _i, _i, _c.c_float, _i, _p, _i64, _p, _p, _p, _p, _p, _p, _p]),
     "qmoe_prefill_workspace_bytes": (_sz, [_i, _i, _i, _i]),

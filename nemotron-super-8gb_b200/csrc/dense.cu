@@ -38,13 +38,17 @@ static int launch_dense_v(const GemvArgs &g, cudaStream_t st, int dev, const Dev
 
 template <int FMT, int CPL>
 static int launch_dense_m(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
-    return g.x_dtype == QMOE_DT_F32 ? launch_dense_v<FMT, CPL, true>(g, st, dev, di)
-                                    : launch_dense_v<FMT, CPL, false>(g, st, dev, di);
+    if constexpr (FMT == 2) {
+        return launch_dense_v<FMT, CPL, true>(g, st, dev, di);
+    } else {
+        return g.x_dtype == QMOE_DT_F32 ? launch_dense_v<FMT, CPL, true>(g, st, dev, di)
+                                        : launch_dense_v<FMT, CPL, false>(g, st, dev, di);
+    }
 }
 
 template <int FMT>
 static int launch_dense(const GemvArgs &g, cudaStream_t st, int dev, const DeviceInfo &di) {
-    const int nch = (FMT == 1 ? g.K / 2 : g.K) / 16;
+    const int nch = (FMT == 1 ? g.K / 2 : FMT == 2 ? g.K * 2 : g.K) / 16;
     const int need = (nch + 31) / 32;
     if (need <= 2) return launch_dense_m<FMT, 2>(g, st, dev, di);
     if (need <= 4) return launch_dense_m<FMT, 4>(g, st, dev, di);
@@ -149,6 +153,28 @@ int dq_gemv_nvfp4_bf16(const uint8_t *w, const uint8_t *sc, const float *s2, con
     g.ybf = y;
     g.res = residual;
     return launch_dense<1>(g, as_stream(stream), dev, *di);
+}
+
+int dq_gemv_bf16(const uint16_t *w, const void *x, int x_dtype, int M, int N, int K, int epilogue,
+                 const uint16_t *residual, uint16_t *y, void *stream) {
+    if (!w || !x || !y || (epilogue == 2 && !residual)) return QMOE_ERR_NULL;
+    if (epilogue < 0 || epilogue > 2 || M < 1 || M > 4 || N < 1 || K < 8 || (K % 8)) return QMOE_ERR_SHAPE;
+    if (!aligned16(w)) return QMOE_ERR_ALIGN;
+    if (!valid_dtype(x_dtype)) return QMOE_ERR_DTYPE;
+    int dev;
+    DeviceInfo *di;
+    if (int e = current_device(&dev, &di)) return e;
+    GemvArgs g{};
+    g.w = reinterpret_cast<const uint8_t *>(w);
+    g.x = x;
+    g.x_dtype = x_dtype;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.out_op = epilogue == 0 ? 3 : epilogue;
+    g.ybf = y;
+    g.res = residual;
+    return launch_dense<2>(g, as_stream(stream), dev, *di);
 }
 
 int dq_dequant_rows(int fmt, const uint8_t *w, const uint8_t *sc, const float *s, int64_t N, int64_t K, int64_t r0,

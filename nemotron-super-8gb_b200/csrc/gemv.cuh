@@ -54,11 +54,13 @@ constexpr int GEMV_WARPS = GEMV_THREADS / 32;
 // The vector of a GEMV in shared memory: f16x2 (bf16 / f16 activations, prescaled) or fp32.
 __host__ __device__ constexpr int gemv_vec_bytes(bool vf32) { return vf32 ? 4 : 2; }
 
-// FMT 0 = FP8 e4m3 (16 elements per 16-byte chunk), 1 = NVFP4 (32 elements per chunk, 2 scales).
+// FMT 0 = FP8 e4m3 (16 elements per 16-byte chunk), 1 = NVFP4 (32 elements per chunk, 2 scales), 2 = bf16 (8
+// elements per chunk, no scale; always with fp32 vectors, the bf16 weights widened exactly).
 // VF32: the vectors are staged (and multiplied) in fp32; otherwise as prescaled f16.
 template <int FMT, int MODE, int CPL, int M, bool VF32>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows_per_cta) {
-    constexpr int EPC = FMT == 1 ? 32 : 16;          // elements per chunk
+    constexpr int EPC = FMT == 1 ? 32 : FMT == 2 ? 8 : 16;   // elements per chunk
+    static_assert(FMT != 2 || VF32, "bf16 weights take fp32 vectors");
     constexpr int EPU = VF32 ? 4 : 8;                 // vector elements per uint4
     constexpr int Q = EPC / EPU;                      // uint4 of the vector per chunk
     extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -67,7 +69,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
     __shared__ float vscale[M];
 
     const int K = a.K;
-    const int KB = FMT == 1 ? K / 2 : K;
+    const int KB = FMT == 1 ? K / 2 : FMT == 2 ? K * 2 : K;
     const int nch = KB / 16;   // chunks per row
     const int item = blockIdx.y;
     const int row0 = blockIdx.x * rows_per_cta;
@@ -82,7 +84,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
     if (MODE == GM_DENSE) {
         W = a.w;
         S = a.sc;
-        mult = *a.s;
+        mult = FMT == 2 ? 1.f : *a.s;
     } else {
         int64_t slot = a.sidx[item];
         bad = slot < 0 || slot >= a.nslots;
@@ -219,6 +221,14 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a, int rows
                                 const float2 sf = __half22float2(as_h2(e4m3x2_f16x2(sv[rr][i])));
                                 acc[rr][m] = fmaf(g[0][0] + g[0][1], sf.x, acc[rr][m]);
                                 acc[rr][m] = fmaf(g[1][0] + g[1][1], sf.y, acc[rr][m]);
+                            } else if (FMT == 2) {
+#pragma unroll
+                                for (int wd = 0; wd < 4; ++wd) {   // word wd: elements 2wd, 2wd+1 (bf16 -> fp32 exact)
+                                    const float2 xv = xf[wd];
+                                    g[0][0] = fmaf(__uint_as_float(ww[wd] << 16), xv.x, g[0][0]);
+                                    g[0][1] = fmaf(__uint_as_float(ww[wd] & 0xFFFF0000u), xv.y, g[0][1]);
+                                }
+                                acc[rr][m] += g[0][0] + g[0][1];
                             } else {
 #pragma unroll
                                 for (int wd = 0; wd < 4; ++wd) {   // word wd: elements 4wd .. 4wd+3

@@ -27,9 +27,18 @@ from expert_store import RoutedExperts
 
 def linear(w, x):
     """x [..., K] -> [..., N] in x.dtype: a dense_q quantized-weight dict (FP8 / NVFP4, dense_q.py:237-247)
-    runs the B200 GEMV kernels; a plain [N, K] tensor runs F.linear."""
+    runs the B200 GEMV kernels; a plain bf16 [N, K] weight with one bf16 row of x runs the bf16 GEMV
+    (dq_gemv_bf16: fp32 accumulation, bf16 result, as F.linear up to the order of the fp32 sums); otherwise
+    F.linear."""
     if isinstance(w, dict):
         return D.qlinear(w, x)
+    if (w.dtype == torch.bfloat16 and x.dtype == torch.bfloat16 and w.dim() == 2 and w.is_contiguous()
+            and x.numel() == x.shape[-1] and w.shape[1] % 8 == 0 and w.shape[1] == x.shape[-1]):
+        x1 = x.reshape(1, -1).contiguous()
+        y = torch.empty(1, w.shape[0], dtype=torch.bfloat16, device=x.device)
+        C.call("dq_gemv_bf16", C.ptr(w), C.ptr(x1), C.dtype_code(x1), 1, w.shape[0], w.shape[1], 0, None, C.ptr(y),
+               C.stream_of(x1))
+        return y.view(*x.shape[:-1], w.shape[0])
     return F.linear(x, w.to(x.dtype))
 
 

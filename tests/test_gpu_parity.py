@@ -625,3 +625,28 @@ def test_route_decode_shapes_and_ties(ne, k):
     bias.zero_()
     o = run(flat)
     assert o["ids"].tolist() == list(range(k))
+
+
+@pytest.mark.parametrize("N,K,M", [(4096, 1024, 1), (1024, 4096, 1), (1000, 4104, 3)])
+def test_bf16_gemv(N, K, M):
+    """dq_gemv_bf16 (bf16 weights widened exactly, fp32 accumulation, bf16 result) against the fp64 product rounded
+    to bf16: within one bf16 rounding (rel-L2 <= 2^-8, nearly every element equal); its relu^2 and residual
+    epilogues equal torch's bf16 operators applied to its plain result, bit for bit."""
+    import _qmoe_lib as C
+    g = torch.Generator(device=DEV).manual_seed(N + K + M)
+    w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+    res = torch.randn(M, N, generator=g, device=DEV).to(torch.bfloat16)
+    outs = {}
+    for ep in (0, 1, 2):
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        C.call("dq_gemv_bf16", C.ptr(w), C.ptr(x), C.dtype_code(x), M, N, K, ep, C.ptr(res) if ep == 2 else None,
+               C.ptr(y), C.stream_of(x))
+        outs[ep] = y
+    ref = (x.double() @ w.double().t())
+    y0 = outs[0]
+    assert rel_l2(y0.float().cpu().numpy(), ref.cpu().numpy()) < 2.0 ** -8
+    assert (y0 == ref.to(torch.bfloat16)).float().mean().item() > 0.99
+    u = torch.relu(y0)
+    assert torch.equal(outs[1], u * u)
+    assert torch.equal(outs[2], y0 + res)
