@@ -43,6 +43,7 @@ extern "C" {
 #define QMOE_DT_F32 0
 #define QMOE_DT_BF16 1
 #define QMOE_DT_F16 2
+#define QMOE_DT_F32_AS_BF16 3  /* dq_gemv_bf16 only: fp32 values, each rounded to bf16 as it is read */
 
 #define QMOE_LAT 1024
 #define QMOE_INTER 2688
@@ -246,7 +247,8 @@ int dq_gemv_nvfp4(const uint8_t *w, const uint8_t *sc, const float *s2, const vo
  * block, nem_super.py:376-377, run through torch's F.linear): y [M, N] bf16 = bf16 weights w [N, K] times x [M, K]
  * (bf16, f16 or fp32), the weights widened to fp32 exactly and every product accumulated in fp32, then rounded to
  * bf16 with the same epilogues as dq_gemv_nvfp4_bf16 (0: the result; 1: relu^2; 2: + residual). 1 <= M <= 4,
- * K % 8 == 0, w 16-byte aligned. */
+ * K % 8 == 0, w 16-byte aligned. x_dtype may also be QMOE_DT_F32_AS_BF16: fp32 x rounded to bf16 on load, the
+ * same values as a bf16 cast of x before the call (the MoE block's routed output y before fc2_latent_proj). */
 int dq_gemv_bf16(const uint16_t *w, const void *x, int x_dtype, int M, int N, int K, int epilogue,
                  const uint16_t *residual, uint16_t *y, void *stream);
 

@@ -99,6 +99,8 @@ __device__ __forceinline__ float h2sum_f32(__half2 a) {
 __device__ __forceinline__ float load_act(const void *p, int dt, int64_t i) {
     if (dt == QMOE_DT_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(p)[i]);
     if (dt == QMOE_DT_F16) return __half2float(reinterpret_cast<const __half *>(p)[i]);
+    if (dt == QMOE_DT_F32_AS_BF16)
+        return __bfloat162float(__float2bfloat16_rn(reinterpret_cast<const float *>(p)[i]));
     return reinterpret_cast<const float *>(p)[i];
 }
 

@@ -160,7 +160,7 @@ int dq_gemv_bf16(const uint16_t *w, const void *x, int x_dtype, int M, int N, in
     if (!w || !x || !y || (epilogue == 2 && !residual)) return QMOE_ERR_NULL;
     if (epilogue < 0 || epilogue > 2 || M < 1 || M > 4 || N < 1 || K < 8 || (K % 8)) return QMOE_ERR_SHAPE;
     if (!aligned16(w)) return QMOE_ERR_ALIGN;
-    if (!valid_dtype(x_dtype)) return QMOE_ERR_DTYPE;
+    if (!valid_dtype(x_dtype) && x_dtype != QMOE_DT_F32_AS_BF16) return QMOE_ERR_DTYPE;
     int dev;
     DeviceInfo *di;
     if (int e = current_device(&dev, &di)) return e;

@@ -154,7 +154,15 @@ class MoELayer(torch.nn.Module):
         cur.wait_event(lat_ready)
         ex = self.experts
         y = Q.moe_decode_groups(ex.store.blocks, sidx, tab, s2, coef, lat[0], ex.h, ex.part, ex.gidx, ex.gcnt)
-        out = linear(self.fc2, y.view(1, -1).to(lat.dtype))
+        w2 = self.fc2
+        if (isinstance(w2, torch.Tensor) and w2.dtype == torch.bfloat16 and lat.dtype == torch.bfloat16
+                and w2.is_contiguous() and w2.shape[1] % 8 == 0):
+            # fc2 on y's fp32 values rounded to bf16 as they are read (the values of y.to(bf16), without the cast)
+            out = torch.empty(1, w2.shape[0], dtype=torch.bfloat16, device=x.device)
+            C.call("dq_gemv_bf16", C.ptr(w2), C.ptr(y), 3, 1, w2.shape[0], w2.shape[1], 0, None, C.ptr(out),
+                   cur.cuda_stream)
+        else:
+            out = linear(self.fc2, y.view(1, -1).to(lat.dtype))
         cur.wait_stream(side)
         if not torch.cuda.is_current_stream_capturing():   # made on the side stream, read on this one
             lat.record_stream(cur)

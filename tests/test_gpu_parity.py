@@ -650,3 +650,11 @@ def test_bf16_gemv(N, K, M):
     u = torch.relu(y0)
     assert torch.equal(outs[1], u * u)
     assert torch.equal(outs[2], y0 + res)
+    # fp32 x rounded to bf16 as it is read (x_dtype 3) = the bf16 cast of x before the call
+    xf = x.float() + 1e-3 * torch.randn(M, K, generator=g, device=DEV)
+    y3 = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    yc = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    xc = xf.to(torch.bfloat16)
+    C.call("dq_gemv_bf16", C.ptr(w), C.ptr(xf), 3, M, N, K, 0, None, C.ptr(y3), C.stream_of(x))
+    C.call("dq_gemv_bf16", C.ptr(w), C.ptr(xc), C.dtype_code(xc), M, N, K, 0, None, C.ptr(yc), C.stream_of(x))
+    assert torch.equal(y3, yc)
