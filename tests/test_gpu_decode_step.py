@@ -158,3 +158,24 @@ def test_fused_shared_expert_is_bit_identical(model):
         finally:
             del layer._fused_shared
         assert torch.equal(fused, plain)
+
+
+def test_bf16_projection_layer_is_bit_identical(model):
+    """A layer whose latent projections are plain bf16 weights (as the reference's fc1 / fc2_latent_proj): the
+    one-token path (fc1 on the side stream, fc2 reading y rounded to bf16 on load, the add in fc2's epilogue)
+    equals the plain composition (bf16 GEMVs, y.to(bf16), the unfused shared expert, the add) bit for bit."""
+    import decode_step as DS
+    base = model["layers"][1]
+    g = model["g"]
+    fc1 = (torch.randn(LAT, H, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    fc2 = (torch.randn(H, LAT, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    layer = DS.MoELayer(1, base.experts.store, base.gate_w, base.bias, fc1, fc2, base.shared_up, base.shared_down)
+    for t in range(3):
+        x = torch.randn(1, H, generator=g, device=DEV).to(torch.bfloat16)
+        fused = layer(x).clone()
+        layer._fused_shared = lambda *a: False
+        try:
+            plain = layer(x).clone()
+        finally:
+            del layer._fused_shared
+        assert torch.equal(fused, plain)
