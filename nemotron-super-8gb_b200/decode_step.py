@@ -137,7 +137,8 @@ class MoELayer(torch.nn.Module):
         cur = torch.cuda.current_stream(x.device)
         side = self._side.get(x.device.index)
         if side is None:
-            side = self._side[x.device.index] = torch.cuda.Stream(x.device)
+            # high priority: its small GEMVs go ahead of pending CTAs of the routed layer kernel
+            side = self._side[x.device.index] = torch.cuda.Stream(x.device, priority=-1)
         su, sd = self.shared_up, self.shared_down
         side.wait_stream(cur)
         with torch.cuda.stream(side):
