@@ -658,3 +658,40 @@ def test_bf16_gemv(N, K, M):
     C.call("dq_gemv_bf16", C.ptr(w), C.ptr(xf), 3, M, N, K, 0, None, C.ptr(y3), C.stream_of(x))
     C.call("dq_gemv_bf16", C.ptr(w), C.ptr(xc), C.dtype_code(xc), M, N, K, 0, None, C.ptr(yc), C.stream_of(x))
     assert torch.equal(y3, yc)
+
+
+def test_new_entry_points_at_their_edges(D, synth):
+    """The bf16-result GEMVs at M = 3 and 4 and with f16 / fp32 vectors, and the routing kernel with one expert and
+    top-1: each against the same computation by torch on the same values."""
+    import _qmoe_lib as C
+    g = synth.seeded(909, DEV)
+    N, K = 512, 1024
+    codes, sc, s2 = synth.quantize_nvfp4(torch.randn(N, K, generator=g, device=DEV) * 0.02)
+    q = {"fmt": "nvfp4", "w": codes, "sc": sc, "s": s2.reshape(1), "N": N, "K": K}
+    for M in (3, 4):
+        x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
+        v = D.gemv_mb(q, x)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        C.call("dq_gemv_nvfp4_bf16", C.ptr(codes), C.ptr(sc), C.ptr(q["s"]), C.ptr(x), C.dtype_code(x), M, N, K, 1,
+               None, C.ptr(y), C.stream_of(x))
+        u = torch.relu(v.to(torch.bfloat16))
+        assert torch.equal(y, u * u), M
+    wb = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
+    for xdt in (torch.float16, torch.float32):
+        x = torch.randn(2, K, generator=g, device=DEV).to(xdt)
+        y = torch.empty(2, N, dtype=torch.bfloat16, device=DEV)
+        C.call("dq_gemv_bf16", C.ptr(wb), C.ptr(x), C.dtype_code(x), 2, N, K, 0, None, C.ptr(y), C.stream_of(x))
+        ref = (x.double() @ wb.double().t())
+        assert rel_l2(y.float().cpu().numpy(), ref.cpu().numpy()) < 2.0 ** -8, xdt
+    logits = torch.randn(1, device=DEV)
+    bias = torch.zeros(1, device=DEV)
+    s2r = torch.rand(1, 2, device=DEV)
+    blocks = torch.empty(1, 16, dtype=torch.uint8, device=DEV)
+    o = dict(ids=torch.empty(1, dtype=torch.int64, device=DEV), sidx=torch.empty(1, dtype=torch.int32, device=DEV),
+             tab=torch.empty(1, dtype=torch.int64, device=DEV), s2=torch.empty(1, 2, device=DEV),
+             coef=torch.empty(1, device=DEV))
+    C.call("qmoe_route_decode", C.ptr(logits), C.ptr(bias), 1, 1, 1.0, 0, C.ptr(blocks), 16, C.ptr(s2r),
+           C.ptr(o["ids"]), C.ptr(o["sidx"]), C.ptr(o["tab"]), C.ptr(o["s2"]), C.ptr(o["coef"]), C.stream_of(logits))
+    torch.cuda.synchronize()
+    assert int(o["ids"]) == 0 and int(o["sidx"]) == 0 and int(o["tab"]) == blocks.data_ptr()
+    assert torch.equal(o["coef"], logits.sigmoid()) and torch.equal(o["s2"], s2r)
